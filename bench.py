@@ -1,0 +1,371 @@
+"""Benchmark of the paged KV-cache decode path (BASELINE config 3 / 5).
+
+Workload: Qwen3-4B layer shape (Hq=32, Hkv=8, D=128, bf16), 36 layers, each
+with 32768 cached tokens in a fragmented block table over a 4096-page pool
+(seeded permutation; synthetic N(0,1) values — the reference has no dataset).
+A step is one decode token through all 36 layers: per layer one fused launch
+that appends the token's K/V into its page and attends over the 32k+ tokens
+(split-K flash-decoding + split combine). The KV data of a step (36 x 128 MiB)
+is far larger than L2 (126 MB), so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N>1 (launched by torch.distributed.run, one rank per GPU): the 8 KV heads are
+sharded over the ranks (8/N each, the matching query heads with them), block
+tables are identical on every rank, and each layer's outputs are all-gathered
+with NCCL. Total work is fixed as N grows (strong scaling).
+
+--impl reference times the reference's own CPU op (oracle/_ref, compiled from
+the Genllm sources; else the C restatement) on the host cores on the same
+config: one process, one thread per layer (the op itself is single-threaded).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged-attn decode HBM GB/s (% of 8 TB/s) @32k ctx; tok/s Qwen3-4B-shape"
+UNIT = "GB/s"
+NOMINAL_HBM_GBS = 8000.0
+HQ, HKV, D, LAYERS, CTX, POOL = 32, 8, 128, 36, 32768, 4096
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
+    return ap.parse_args()
+
+
+def config(args, world):
+    return {"workload": "Qwen3-4B layer-shape paged-attention decode, 36 layers back to back",
+            "n_q_heads": HQ, "n_kv_heads": HKV, "head_dim": D, "layers": args.layers, "ctx": args.ctx,
+            "page_size": 16, "pool_pages": POOL, "block_table": "seeded random permutation (fragmented)",
+            "batch": 1, "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (36 x 128 MiB of KV per step), no flush"}
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region (NVML polling thread)
+class ClockSampler:
+    def __init__(self, index):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    _NAMES = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+              0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+              0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(0.005)
+
+    def sample(self):
+        if not self.nv:
+            return
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self._NAMES.items():
+                if r & bit and name != "gpu_idle":
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def start(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+        self.sample()
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+# --------------------------------------------------------------------------
+def run_reference_arm(args, rank, world):
+    """The reference's CPU implementation of the path, timed alone."""
+    if rank != 0:
+        return
+    vals, dts, byts = [], [], []
+    info = None
+    for i in range(args.warmup + args.steps):
+        g, cores, kind, sample, dt, nbytes = cpu_step(args)
+        info = (cores, kind, sample)
+        if i >= args.warmup:
+            dts.append(dt)
+            byts.append(nbytes)
+    value = sum(byts) / sum(dts) / 1e9
+    cores, kind, sample = info
+    line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * sum(dts) / len(dts), 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config(args, world), "impl": "reference",
+            "frac_of_8TBps": round(value / NOMINAL_HBM_GBS, 6),
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+_cpu = {}
+
+
+def cpu_step(args):
+    """One timed step of the reference CPU op on the host: one decode token
+    (append + attention) of T layers at once, one host thread per layer (the
+    op itself is single-threaded; distinct layers share no state), T = the
+    host's cores, at most the config's 36 layers. Falls back to the C
+    restatement (one layer, threads over its heads) when oracle/_ref is absent.
+    Returns (GB/s, cores, kind, sample, seconds, algorithmic bytes)."""
+    import numpy as np
+    from genllm_b200.synth import bf16_bits
+    from oracle.oracle import Oracle, RefSession, ref_available
+
+    c = _cpu
+    if not c:
+        T = max(1, min(os.cpu_count() or 1, args.layers))
+        n_pages = (args.ctx + 15) // 16
+        pool = n_pages + 64
+        tile = bf16_bits(np.random.default_rng(0).standard_normal(1 << 20, dtype=np.float32))
+        c.update(T=T, n_pages=n_pages, pool=pool, tile=tile, ctx=args.ctx)
+        c["q"] = [np.resize(tile, HQ * D).reshape(HQ, 1, D).copy() for _ in range(T)]
+        c["kv"] = [np.resize(tile[7:], HKV * D).reshape(HKV, 1, D).copy() for _ in range(T)]
+        c["out"] = [np.zeros((HQ, 1, D), np.uint16) for _ in range(T)]
+        if ref_available():
+            s = RefSession(T, HKV, D, pool)
+            for l in range(T):
+                for w in (0, 1):
+                    view = s.pool_view(l, w).reshape(-1)
+                    view[:] = np.resize(tile, view.size)
+                    for _ in range(pool):
+                        s.alloc(l, w)
+                    for pid in range(pool - 1, n_pages - 1, -1):
+                        s.free(l, w, pid)
+                ids = np.random.default_rng(l).permutation(n_pages).astype(np.int32)
+                s.set_table(l, ids, ids, args.ctx)
+            c.update(s=s, kind="reference", layers=T,
+                     sample=(f"{T} layers at once (one host thread each; the op is single-threaded), one decode "
+                             f"token per layer per step, ctx {args.ctx} and growing, reference CPU op "
+                             f"(ops::PagedAttentionImpl<CPU>::execute) built from the Genllm sources"))
+        else:
+            c.update(s=None, kind="port", layers=1, o=Oracle(), kp=np.resize(tile, pool * 16 * HKV * D),
+                     ids=np.random.default_rng(0).permutation(pool)[: n_pages + 1].astype(np.int32),
+                     sample=f"one layer-token at ctx {args.ctx}, C restatement over {T} threads")
+    total = c["ctx"] + 1
+    if c["s"] is not None:
+        t0 = time.perf_counter()
+        c["s"].paged_attention_layers(c["q"], c["kv"], c["kv"], c["out"], HQ, 1, 1 / np.sqrt(D))
+        dt = time.perf_counter() - t0
+        c["ctx"] += 1
+    else:
+        t0 = time.perf_counter()
+        c["o"].paged_attention_f32(c["q"][0], c["kp"], c["kp"], c["ids"], c["ids"], total, HQ, HKV, 1, D,
+                                   1 / np.sqrt(D), threads=c["T"])
+        dt = time.perf_counter() - t0
+    per_layer = 2 * (total - 1) * HKV * D * 2 + 2 * 2 * HKV * D * 2 + 2 * HQ * D * 2 + ((total + 15) // 16) * 8
+    nbytes = c["layers"] * per_layer
+    return nbytes / dt / 1e9, c["T"], c["kind"], c["sample"], dt, nbytes
+
+
+# --------------------------------------------------------------------------
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from genllm_b200.workload import DecodeWorkload
+
+    wl = DecodeWorkload(local, n_layers=args.layers, ctx=args.ctx, pool_pages=POOL, n_q_heads=HQ, n_kv_heads=HKV,
+                        head_dim=D, seed=0, world=world, rank=rank)
+    stream = torch.cuda.current_stream()
+    sh = __import__("ctypes").c_void_p(stream.cuda_stream)
+    gathered = [torch.empty((1, HQ, 1, D), dtype=torch.bfloat16, device="cuda") for _ in range(args.layers)]
+
+    def step(events=None):
+        for l in range(args.layers):
+            if events is not None:
+                events[l][0].record(stream)
+            wl.layer_step(l, sh)
+            if events is not None:
+                events[l][1].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered[l].view(world, -1), wl.layers[l].out.view(-1))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx0 = wl.cached(0)
+
+    ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(args.layers)]
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(ev[k])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = t_start.elapsed_time(t_end)
+    kern_ms = [ev[k][l][0].elapsed_time(ev[k][l][1]) for k in range(args.steps) for l in range(args.layers)]
+    kern_avg_ms = sum(kern_ms) / len(kern_ms)
+
+    # Algorithmic bytes: this rank's launches over the timed steps.
+    byts = 0
+    for k in range(args.steps):
+        byts += args.layers * wl.bytes_per_layer_token(ctx0 + k + 1)
+    per_launch_bytes = byts / (args.steps * args.layers)
+    t = torch.tensor([ms, kern_avg_ms], device="cuda")
+    b = torch.tensor([float(byts)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+    ms_max, kern_max = t.tolist()
+    total_bytes = b.item()
+    value = total_bytes / (ms_max / 1e3) / 1e9
+
+    # ---- end to end: host buffers through the public API ---------------
+    e2e_steps = args.e2e_steps or args.steps
+    from genllm_b200.paged_attention import paged_attention
+    hq_l, hkv_l = wl.hq_local, wl.hkv_local
+    hq_in = [torch.empty((1, hq_l, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(args.layers)]
+    hk_in = [torch.empty((1, hkv_l, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(args.layers)]
+    hv_in = [torch.empty((1, hkv_l, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(args.layers)]
+    h_out = [torch.empty((1, HQ if world > 1 else hq_l, 1, D), dtype=torch.bfloat16).pin_memory()
+             for _ in range(args.layers)]
+    for l in range(args.layers):
+        hq_in[l].copy_(wl.layers[l].q)
+        hk_in[l].copy_(wl.layers[l].k)
+        hv_in[l].copy_(wl.layers[l].v)
+
+    def e2e_step():
+        for l in range(args.layers):
+            L = wl.layers[l]
+            L.q.copy_(hq_in[l], non_blocking=True)
+            L.k.copy_(hk_in[l], non_blocking=True)
+            L.v.copy_(hv_in[l], non_blocking=True)
+            paged_attention(wl.mgr, l, L.q, L.k, L.v, out=L.out, scale=wl.scale)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered[l].view(world, -1), L.out.view(-1))
+                h_out[l].copy_(gathered[l], non_blocking=True)
+            else:
+                h_out[l].copy_(L.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(h_out[-1].view(-1)[0])  # the step's result, read on the host
+
+    for _ in range(2):
+        e2e_step()
+    ctx1 = wl.cached(0)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    eb = 0
+    for k in range(e2e_steps):
+        eb += args.layers * wl.bytes_per_layer_token(ctx1 + k + 1)
+    te = torch.tensor([e_ms], device="cuda")
+    be = torch.tensor([float(eb)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        dist.all_reduce(be, op=dist.ReduceOp.SUM)
+    e2e_value = be.item() / (te.item() / 1e3) / 1e9
+    h2d = args.layers * (hq_in[0].numel() + hk_in[0].numel() + hv_in[0].numel()) * 2
+    d2h = args.layers * h_out[0].numel() * 2
+
+    peak, peak_src = measured_peak()
+    achieved = per_launch_bytes / (kern_max / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config(args, world),
+        "frac_of_8TBps": round(value / NOMINAL_HBM_GBS, 4),
+        "us_per_token_layer": round(1e3 * ms_max / (args.steps * args.layers), 3),
+        "tok_per_s_qwen3_4b_attention": round(args.steps / (ms_max / 1e3), 2),
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "ms_per_step": round(te.item() / e2e_steps, 4),
+                "path": "pinned host Q/K/V -> device, genllm_b200.paged_attention (C ABI), device -> host output"},
+        "gpu_launches": args.steps * args.layers,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "kernel": "paged_decode_kernel<4>", "kernel_avg_us": round(1e3 * kern_max, 3),
+                     "bytes_per_launch": round(per_launch_bytes)},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_step(args)  # warm-up (and set-up) step, untimed
+        runs = [cpu_step(args) for _ in range(3)]
+        g = sum(r[5] for r in runs) / sum(r[4] for r in runs) / 1e9
+        _, cores, kind, sample, _, _ = runs[0]
+        line["cpu_baseline"] = {"value": round(g, 4), "unit": UNIT, "cores": cores, "kind": kind,
+                                "sample": sample + "; 3 timed steps after one untimed",
+                                "seconds_per_step": round(sum(r[4] for r in runs) / 3, 3)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,879 @@
+// host.cpp — the C ABI (include/genllm_kv.h): page allocators, block tables,
+// layer state and kernel dispatch for the B200 paged KV-cache path.
+//
+// Mirrors the reference's BlockPool / PagedAttentionManager
+// (include/core/page_attention.h:11-89, src/core/page_attention.cpp:25-216)
+// and replaces PagedAttentionImpl<Device::CUDA>::execute
+// (src/backend/cuda/attention.cu:491-580). The differences are deliberate:
+//   * the block table lives on the device and is updated incrementally by the
+//     kernels themselves (new entries ride in the launch parameters), instead
+//     of a cudaMalloc + H2D + cudaFree of the whole table per call;
+//   * an exhausted pool is an error (GKV_ERR_NO_PAGES) that leaves the layer
+//     unchanged, where the reference keeps counting tokens and later indexes
+//     its table out of bounds (page_attention.cpp:155,161,127);
+//   * all work is enqueued on the caller's stream; nothing synchronises.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <climits>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/genllm_kv.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(GKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Runs the body with `device` current and restores the caller's device.
+class DeviceGuard {
+   public:
+    explicit DeviceGuard(int device) {
+        ok_ = cudaGetDevice(&prev_) == cudaSuccess;
+        if (ok_ && prev_ != device) ok_ = cudaSetDevice(device) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+    }
+    bool ok() const { return ok_; }
+
+   private:
+    int prev_ = 0;
+    bool ok_ = false;
+};
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library needs no link-time dependency on libcuda.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool is_out_dtype(int d) { return d == GKV_F32 || d == GKV_F16 || d == GKV_BF16; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+namespace gkv {
+
+bool encode_pool_maps(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    // dims (fastest first): head dim, kv head, slot row over the whole pool.
+    cuuint64_t dims[3] = {(cuuint64_t)gkv::kHeadDim, (cuuint64_t)pool.n_kv_heads,
+                          (cuuint64_t)pool.pool_pages * 16};
+    cuuint64_t strides[2] = {(cuuint64_t)gkv::kHeadDim * 2,
+                             (cuuint64_t)pool.n_kv_heads * gkv::kHeadDim * 2};
+    cuuint32_t box[3] = {(cuuint32_t)gkv::kHeadDim, 1, 16};
+    cuuint32_t estr[3] = {1, 1, 1};
+    for (int i = 0; i < 2; ++i) {
+        CUtensorMap* m = i == 0 ? k_map : v_map;
+        void* base = i == 0 ? pool.k_base : pool.v_base;
+        CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            *why = "cuTensorMapEncodeTiled failed";
+            return false;
+        }
+    }
+    return true;
+}
+
+}  // namespace gkv
+
+// ============================ raw tier ======================================
+
+struct gkv_table {
+    int device = 0;
+    int32_t capacity = 0;
+    int num_sms = 148;
+    int2* d_table = nullptr;
+    gkv::Scratch scratch{};
+    // Tensor maps cached for the last pool seen.
+    void* map_k_base = nullptr;
+    void* map_v_base = nullptr;
+    int32_t map_pages = -1;
+    int32_t map_heads = -1;
+    CUtensorMap k_map;
+    CUtensorMap v_map;
+};
+
+namespace {
+
+void table_free(gkv_table* t) {
+    cudaFree(t->d_table);
+    cudaFree(t->scratch.part_acc);
+    cudaFree(t->scratch.part_ml);
+    cudaFree(t->scratch.counters);
+    cudaFree(t->scratch.err);
+}
+
+constexpr int kMaxKvHeads = 256;
+
+int check_pool(const gkv_pool_desc* pool) {
+    if (!pool) return fail(GKV_ERR_INVALID, "null pool descriptor");
+    if (pool->head_dim != 128)
+        return fail(GKV_ERR_UNSUPPORTED, "head_dim %d: only 128 is built", pool->head_dim);
+    if (pool->dtype != GKV_BF16)
+        return fail(GKV_ERR_UNSUPPORTED, "KV dtype %d: only bf16 (30) is built", pool->dtype);
+    if (pool->n_kv_heads < 1 || pool->n_kv_heads > kMaxKvHeads)
+        return fail(GKV_ERR_INVALID, "n_kv_heads %d out of range", pool->n_kv_heads);
+    if (pool->pool_pages < 1) return fail(GKV_ERR_INVALID, "pool_pages %d", pool->pool_pages);
+    if (!pool->k_base || !pool->v_base || !aligned16(pool->k_base) || !aligned16(pool->v_base))
+        return fail(GKV_ERR_INVALID, "pool bases must be non-null and 16-byte aligned");
+    return GKV_OK;
+}
+
+int table_maps(gkv_table* t, const gkv_pool_desc* pool) {
+    if (t->map_k_base == pool->k_base && t->map_v_base == pool->v_base &&
+        t->map_pages == pool->pool_pages && t->map_heads == pool->n_kv_heads)
+        return GKV_OK;
+    gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
+                     pool->pool_pages, pool->n_kv_heads};
+    const char* why = nullptr;
+    if (!gkv::encode_pool_maps(pv, &t->k_map, &t->v_map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
+    t->map_k_base = pool->k_base;
+    t->map_v_base = pool->v_base;
+    t->map_pages = pool->pool_pages;
+    t->map_heads = pool->n_kv_heads;
+    return GKV_OK;
+}
+
+// Validate a table delta against a step that ends with n_pages logical pages.
+int check_new_pages(const gkv_table* t, const gkv_new_pages* np, int32_t n_pages, int32_t pool_pages) {
+    if (n_pages > t->capacity)
+        return fail(GKV_ERR_NO_PAGES, "step needs %d table entries, table holds %d", n_pages, t->capacity);
+    if (!np || np->n_new_pages == 0) return GKV_OK;
+    if (np->n_new_pages < 0 || np->first_new_page < 0 || !np->k_ids || !np->v_ids ||
+        np->first_new_page + np->n_new_pages > t->capacity)
+        return fail(GKV_ERR_INVALID, "bad new-page list");
+    for (int i = 0; i < np->n_new_pages; ++i)
+        if (np->k_ids[i] < 0 || np->k_ids[i] >= pool_pages || np->v_ids[i] < 0 || np->v_ids[i] >= pool_pages)
+            return fail(GKV_ERR_INVALID, "new page id out of the pool");
+    return GKV_OK;
+}
+
+gkv::NewPages pack(const gkv_new_pages* np, int32_t from, int32_t n) {
+    gkv::NewPages out;
+    out.first = np ? np->first_new_page + from : 0;
+    out.n = n;
+    for (int i = 0; i < n; ++i) out.ids[i] = make_int2(np->k_ids[from + i], np->v_ids[from + i]);
+    return out;
+}
+
+// Publish new-page entries [from, to) of np with table-only launches.
+int publish(const gkv_pool_desc* pool, gkv_table* t, const gkv_new_pages* np, int32_t from, int32_t to,
+            cudaStream_t s) {
+    gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
+                     pool->pool_pages, pool->n_kv_heads};
+    while (from < to) {
+        const int32_t n = std::min<int32_t>(to - from, gkv::kMaxNewPagesPerLaunch);
+        gkv::NewPages p = pack(np, from, n);
+        cudaError_t e = gkv::launch_append(pv, t->d_table, p, nullptr, nullptr, 0, 0, 0, 0, t->scratch.err, s);
+        if (e != cudaSuccess) return cuda_fail(e, "table publish launch");
+        from += n;
+    }
+    return GKV_OK;
+}
+
+int append_chunks(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
+                  const void* K, const void* V, int32_t seq_len, cudaStream_t s) {
+    gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
+                     pool->pool_pages, pool->n_kv_heads};
+    // Launch in chunks of at most 64 pages (1024 tokens) so that each launch's
+    // new table entries fit in its parameters. Tokens of chunk c live in
+    // logical pages [(n_prior + c0)/16, ...]; entries of the new-page list
+    // that a chunk touches ride with it.
+    const int32_t n_new = np ? np->n_new_pages : 0;
+    const int32_t first_new = np ? np->first_new_page : 0;
+    int32_t published = 0;  // entries of np already sent
+    const int32_t chunk = gkv::kMaxNewPagesPerLaunch * 16 - 16;
+    for (int32_t c0 = 0; c0 < seq_len; c0 += chunk) {
+        const int32_t c1 = std::min(seq_len, c0 + chunk);
+        const int32_t last_page = (n_prior + c1 - 1) / 16;  // inclusive
+        const int32_t upto = std::min(n_new, std::max(published, last_page - first_new + 1));
+        // Entries pending from earlier host-only growth go out first.
+        if (upto - published > gkv::kMaxNewPagesPerLaunch) {
+            const int32_t to = upto - gkv::kMaxNewPagesPerLaunch;
+            const int st = publish(pool, t, np, published, to, s);
+            if (st) return st;
+            published = to;
+        }
+        gkv::NewPages p = pack(np, published, upto - published);
+        cudaError_t e = gkv::launch_append(pv, t->d_table, p, static_cast<const uint16_t*>(K),
+                                           static_cast<const uint16_t*>(V), n_prior, seq_len, c0, c1,
+                                           t->scratch.err, s);
+        if (e != cudaSuccess) return cuda_fail(e, "append launch");
+        published = upto;
+    }
+    if (published < n_new) return publish(pool, t, np, published, n_new, s);
+    return GKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gkv_status_string(int s) {
+    switch (s) {
+        case GKV_OK: return "ok";
+        case GKV_ERR_INVALID: return "invalid argument";
+        case GKV_ERR_NO_PAGES: return "page pool exhausted";
+        case GKV_ERR_CUDA: return "CUDA error";
+        case GKV_ERR_UNSUPPORTED: return "unsupported configuration";
+        case GKV_ERR_STATE: return "layer not initialised or reserved";
+        case GKV_ERR_DEVICE: return "device-side error flagged";
+        default: return "unknown status";
+    }
+}
+
+const char* gkv_last_error(void) { return g_last_error.c_str(); }
+
+int gkv_table_create(int device, int32_t capacity, gkv_table** out) {
+    if (!out || capacity < 1) return fail(GKV_ERR_INVALID, "gkv_table_create: bad arguments");
+    DeviceGuard g(device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", device);
+    auto* t = new gkv_table();
+    t->device = device;
+    t->capacity = capacity;
+    cudaDeviceGetAttribute(&t->num_sms, cudaDevAttrMultiProcessorCount, device);
+    cudaError_t e;
+    if ((e = cudaMalloc(&t->d_table, sizeof(int2) * (size_t)capacity)) != cudaSuccess ||
+        (e = cudaMemset(t->d_table, 0xFF, sizeof(int2) * (size_t)capacity)) != cudaSuccess ||
+        (e = cudaMalloc(&t->scratch.part_acc, sizeof(float) * gkv::kMaxPartialRows * 128)) != cudaSuccess ||
+        (e = cudaMalloc(&t->scratch.part_ml, sizeof(float2) * gkv::kMaxPartialRows)) != cudaSuccess ||
+        (e = cudaMalloc(&t->scratch.counters, sizeof(uint32_t) * kMaxKvHeads)) != cudaSuccess ||
+        (e = cudaMemset(t->scratch.counters, 0, sizeof(uint32_t) * kMaxKvHeads)) != cudaSuccess ||
+        (e = cudaMalloc(&t->scratch.err, sizeof(uint32_t))) != cudaSuccess ||
+        (e = cudaMemset(t->scratch.err, 0, sizeof(uint32_t))) != cudaSuccess) {
+        table_free(t);
+        delete t;
+        return cuda_fail(e, "gkv_table_create");
+    }
+    t->scratch.counters_len = kMaxKvHeads;
+    *out = t;
+    return GKV_OK;
+}
+
+int gkv_table_destroy(gkv_table* t) {
+    if (!t) return GKV_OK;
+    DeviceGuard g(t->device);
+    table_free(t);
+    delete t;
+    return GKV_OK;
+}
+
+const int32_t* gkv_table_device_ptr(const gkv_table* t) {
+    return t ? reinterpret_cast<const int32_t*>(t->d_table) : nullptr;
+}
+
+int gkv_table_check_errors(gkv_table* t, uint32_t* flags) {
+    if (!t) return fail(GKV_ERR_INVALID, "null table");
+    DeviceGuard g(t->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "synchronise");
+    uint32_t v = 0;
+    if ((e = cudaMemcpy(&v, t->scratch.err, 4, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "read error word");
+    if ((e = cudaMemset(t->scratch.err, 0, 4)) != cudaSuccess) return cuda_fail(e, "clear error word");
+    if (flags) *flags = v;
+    return GKV_OK;
+}
+
+int gkv_append_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
+                      const void* K, const void* V, int32_t seq_len, gkv_stream_t stream) {
+    int st = check_pool(pool);
+    if (st) return st;
+    if (!t || n_prior < 0 || seq_len < 0) return fail(GKV_ERR_INVALID, "gkv_append_kv_raw: bad arguments");
+    if (seq_len > 0 && (!K || !V || !aligned16(K) || !aligned16(V)))
+        return fail(GKV_ERR_INVALID, "K/V must be non-null and 16-byte aligned");
+    const int32_t n_pages = (n_prior + seq_len + 15) / 16;
+    if ((st = check_new_pages(t, np, n_pages, pool->pool_pages))) return st;
+    DeviceGuard g(t->device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", t->device);
+    return append_chunks(pool, t, n_prior, np, K, V, seq_len, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
+                            const void* Q, const void* K, const void* V, void* out, int32_t n_q_heads,
+                            int32_t seq_len, float scale, int32_t causal, int32_t out_dtype,
+                            gkv_stream_t stream) {
+    int st = check_pool(pool);
+    if (st) return st;
+    if (!t || n_prior < 0 || seq_len < 1 || !Q || !K || !V || !out)
+        return fail(GKV_ERR_INVALID, "gkv_paged_attention_raw: bad arguments");
+    if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(out))
+        return fail(GKV_ERR_INVALID, "Q/K/V/out must be 16-byte aligned");
+    if (n_q_heads < 1 || n_q_heads % pool->n_kv_heads != 0)
+        return fail(GKV_ERR_INVALID, "n_q_heads %d is not a multiple of n_kv_heads %d", n_q_heads,
+                    pool->n_kv_heads);
+    const int G = n_q_heads / pool->n_kv_heads;
+    if (G != 1 && G != 2 && G != 4 && G != 8)
+        return fail(GKV_ERR_UNSUPPORTED, "group size %d: built for 1, 2, 4, 8", G);
+    if (!is_out_dtype(out_dtype)) return fail(GKV_ERR_UNSUPPORTED, "out dtype %d", out_dtype);
+    const int32_t total = n_prior + seq_len;
+    const int32_t n_pages = (total + 15) / 16;
+    if ((st = check_new_pages(t, np, n_pages, pool->pool_pages))) return st;
+    DeviceGuard g(t->device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", t->device);
+    if ((st = table_maps(t, pool))) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
+                     pool->pool_pages, pool->n_kv_heads};
+
+    if (seq_len == 1) {
+        // Entries beyond the last 64 go first through table-only launches.
+        const int32_t n_new = np ? np->n_new_pages : 0;
+        const int32_t keep = std::min<int32_t>(n_new, gkv::kMaxNewPagesPerLaunch);
+        if (n_new > keep && (st = publish(pool, t, np, 0, n_new - keep, s))) return st;
+        gkv::NewPages p = pack(np, n_new - keep, keep);
+        gkv::DecodeLaunch d{};
+        d.q = static_cast<const uint16_t*>(Q);
+        d.k_new = static_cast<const uint16_t*>(K);
+        d.v_new = static_cast<const uint16_t*>(V);
+        d.out = out;
+        d.out_dtype = out_dtype;
+        d.n_q_heads = n_q_heads;
+        d.n_prior = n_prior;
+        d.total = total;
+        d.n_pages = n_pages;
+        d.scale = scale;
+        d.n_splits = 0;
+        cudaError_t e = gkv::launch_decode(pv, t->k_map, t->v_map, t->d_table, p, t->scratch, d, t->num_sms, s);
+        if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+        return GKV_OK;
+    }
+
+    if ((st = append_chunks(pool, t, n_prior, np, K, V, seq_len, s))) return st;
+    gkv::PrefillLaunch pl{};
+    pl.q = static_cast<const uint16_t*>(Q);
+    pl.out = out;
+    pl.out_dtype = out_dtype;
+    pl.n_q_heads = n_q_heads;
+    pl.seq_len = seq_len;
+    pl.total = total;
+    pl.n_pages = n_pages;
+    pl.scale = scale;
+    pl.causal = causal ? 1 : 0;
+    cudaError_t e = gkv::launch_prefill(pv, t->k_map, t->v_map, t->d_table, pl, t->scratch.err, t->num_sms, s);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+    return GKV_OK;
+}
+
+}  // extern "C"
+
+// ============================ managed tier ==================================
+
+namespace {
+
+// BlockPool (src/core/page_attention.cpp:25-64): ids [0, capacity); alloc
+// takes the most recently freed id, else the next never-used one. Capacity 0
+// means unbounded, as for the reference's default-constructed BlockPool (a
+// layer that was never reserved, page_attention.cpp:44).
+class PagePool {
+   public:
+    void init(int32_t capacity) {
+        capacity_ = capacity;
+        handed_out_ = 0;
+        free_.clear();
+        free_.reserve(capacity);
+        is_free_.assign(capacity, 0);
+    }
+    int32_t capacity() const { return capacity_; }
+    int32_t num_blocks() const { return handed_out_; }
+    int32_t num_free() const { return static_cast<int32_t>(free_.size()); }
+    int32_t available() const {
+        return capacity_ > 0 ? num_free() + (capacity_ - handed_out_) : INT32_MAX;
+    }
+    int32_t alloc() {
+        if (!free_.empty()) {
+            const int32_t id = free_.back();
+            free_.pop_back();
+            is_free_[id] = 0;
+            return id;
+        }
+        if (capacity_ > 0 && handed_out_ >= capacity_) return -1;
+        if (handed_out_ >= static_cast<int32_t>(is_free_.size())) is_free_.push_back(0);
+        return handed_out_++;
+    }
+    // 0 ok / ignored (never handed out), -1 double free.
+    int free(int32_t id) {
+        if (id < 0 || id >= handed_out_) return 0;
+        if (is_free_[id]) return -1;
+        is_free_[id] = 1;
+        free_.push_back(id);
+        return 0;
+    }
+    void reset() {
+        free_.clear();
+        for (int32_t i = 0; i < handed_out_; ++i) free_.push_back(i);
+        std::fill(is_free_.begin(), is_free_.begin() + handed_out_, 1);
+    }
+    bool is_handed_out(int32_t id) const { return id >= 0 && id < handed_out_ && !is_free_[id]; }
+
+   private:
+    int32_t capacity_ = 0;
+    int32_t handed_out_ = 0;
+    std::vector<int32_t> free_;
+    std::vector<uint8_t> is_free_;
+};
+
+struct Layer {
+    bool active = false;
+    bool reserved = false;
+    int32_t num_cached = 0;
+    int32_t n_kv_heads = 0;
+    int32_t head_dim = 0;
+    int32_t dtype = GKV_BF16;
+    int32_t max_blocks = 0;
+    PagePool k_pool, v_pool;
+    std::vector<int32_t> k_ids, v_ids;  // host block table
+    int32_t on_device = 0;              // table entries already published to the device
+    void* k_base = nullptr;
+    void* v_base = nullptr;
+    bool owns_regions = false;
+    gkv_table* table = nullptr;
+};
+
+}  // namespace
+
+struct gkv_manager {
+    int device = 0;
+    std::map<int32_t, Layer> layers;
+};
+
+namespace {
+
+Layer* find_layer(gkv_manager* m, int32_t id) {
+    if (!m) return nullptr;
+    auto it = m->layers.find(id);
+    return it == m->layers.end() ? nullptr : &it->second;
+}
+const Layer* find_layer(const gkv_manager* m, int32_t id) {
+    if (!m) return nullptr;
+    auto it = m->layers.find(id);
+    return it == m->layers.end() ? nullptr : &it->second;
+}
+
+void release_layer(Layer& L) {
+    if (L.owns_regions) {
+        cudaFree(L.k_base);
+        cudaFree(L.v_base);
+    }
+    L.k_base = L.v_base = nullptr;
+    L.owns_regions = false;
+    gkv_table_destroy(L.table);
+    L.table = nullptr;
+    L.reserved = false;
+}
+
+gkv_pool_desc pool_of(const Layer& L) {
+    return gkv_pool_desc{L.k_base, L.v_base, L.max_blocks, L.n_kv_heads, L.head_dim, L.dtype};
+}
+
+// Allocate the pages `count` more tokens need, all or nothing. Returns the
+// first new logical page and how many were added.
+int grow(Layer& L, int32_t count, int32_t* first_new, int32_t* n_new) {
+    int32_t need = 0;
+    for (int32_t p = 0; p < count; ++p)
+        if ((L.num_cached + p) % 16 == 0) ++need;
+    // A table can hold at most max_blocks logical pages.
+    if (L.k_pool.available() < need || L.v_pool.available() < need ||
+        (L.reserved && static_cast<int32_t>(L.k_ids.size()) + need > L.max_blocks))
+        return fail(GKV_ERR_NO_PAGES, "layer needs %d more pages: K pool has %d, V pool has %d", need,
+                    L.k_pool.available(), L.v_pool.available());
+    *first_new = static_cast<int32_t>(L.k_ids.size());
+    *n_new = need;
+    for (int32_t i = 0; i < need; ++i) {
+        L.k_ids.push_back(L.k_pool.alloc());
+        L.v_ids.push_back(L.v_pool.alloc());
+    }
+    return GKV_OK;
+}
+
+void ungrow(Layer& L, int32_t first_new) {
+    while (static_cast<int32_t>(L.k_ids.size()) > first_new) {
+        L.k_pool.free(L.k_ids.back());
+        L.v_pool.free(L.v_ids.back());
+        L.k_ids.pop_back();
+        L.v_ids.pop_back();
+    }
+    L.on_device = std::min<int32_t>(L.on_device, first_new);
+}
+
+// Everything from L.on_device to the end of the table goes to the device with
+// the next launch.
+gkv_new_pages pending(const Layer& L) {
+    gkv_new_pages np;
+    np.first_new_page = L.on_device;
+    np.n_new_pages = static_cast<int32_t>(L.k_ids.size()) - L.on_device;
+    np.k_ids = L.k_ids.data() + L.on_device;
+    np.v_ids = L.v_ids.data() + L.on_device;
+    return np;
+}
+
+// An active layer (page bookkeeping works on it even before reserve_layer,
+// as in the reference's pool-less manager).
+int active_layer(gkv_manager* m, int32_t layer_id, Layer** out) {
+    Layer* L = find_layer(m, layer_id);
+    if (!L || !L->active) return fail(GKV_ERR_STATE, "layer %d is not initialised", layer_id);
+    *out = L;
+    return GKV_OK;
+}
+
+// An active layer with device pools, ready for kernel launches.
+int ready_layer(gkv_manager* m, int32_t layer_id, Layer** out) {
+    int st = active_layer(m, layer_id, out);
+    if (st) return st;
+    if (!(*out)->reserved || !(*out)->table)
+        return fail(GKV_ERR_STATE, "layer %d has no device pools (not reserved, or a host-only manager)",
+                    layer_id);
+    return GKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gkv_manager_create(int device, gkv_manager** out) {
+    if (!out) return fail(GKV_ERR_INVALID, "null out");
+    if (device != -1) {
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+        if (device < 0 || device >= n) return fail(GKV_ERR_INVALID, "device %d of %d", device, n);
+    }
+    auto* m = new gkv_manager();
+    m->device = device;
+    *out = m;
+    return GKV_OK;
+}
+
+int gkv_manager_destroy(gkv_manager* m) {
+    if (!m) return GKV_OK;
+    if (m->device >= 0) {
+        DeviceGuard g(m->device);
+        for (auto& kv : m->layers) release_layer(kv.second);
+    }
+    delete m;
+    return GKV_OK;
+}
+
+int gkv_init_layer(gkv_manager* m, int32_t layer_id, int32_t n_kv_heads, int32_t head_dim, int32_t dtype) {
+    if (!m) return fail(GKV_ERR_INVALID, "null manager");
+    if (n_kv_heads < 1 || n_kv_heads > kMaxKvHeads || head_dim < 1)
+        return fail(GKV_ERR_INVALID, "bad layer geometry");
+    Layer& L = m->layers[layer_id];
+    L.n_kv_heads = n_kv_heads;
+    L.head_dim = head_dim;
+    L.dtype = dtype;
+    L.active = true;
+    L.num_cached = 0;
+    return GKV_OK;
+}
+
+int gkv_reserve_layer(gkv_manager* m, int32_t layer_id, int32_t max_blocks, void* k_region, void* v_region) {
+    Layer* L = find_layer(m, layer_id);
+    if (!L || !L->active) return fail(GKV_ERR_STATE, "layer %d is not initialised", layer_id);
+    if (max_blocks < 1) return fail(GKV_ERR_INVALID, "max_blocks %d", max_blocks);
+    if ((k_region == nullptr) != (v_region == nullptr))
+        return fail(GKV_ERR_INVALID, "give both regions or neither");
+    if (k_region && (!aligned16(k_region) || !aligned16(v_region)))
+        return fail(GKV_ERR_INVALID, "regions must be 16-byte aligned");
+    if (m->device < 0) {
+        // Host-only manager: page bookkeeping with the given capacity, no memory.
+        L->max_blocks = max_blocks;
+        L->k_pool.init(max_blocks);
+        L->v_pool.init(max_blocks);
+        L->k_ids.clear();
+        L->v_ids.clear();
+        L->on_device = 0;
+        L->num_cached = 0;
+        L->reserved = true;
+        return GKV_OK;
+    }
+    const int eb = L->dtype == GKV_F32 ? 4 : 2;
+    const size_t bytes = (size_t)max_blocks * 16 * L->n_kv_heads * L->head_dim * eb;
+    DeviceGuard g(m->device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", m->device);
+    release_layer(*L);
+    if (k_region) {
+        L->k_base = k_region;
+        L->v_base = v_region;
+    } else {
+        cudaError_t e = cudaMalloc(&L->k_base, bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&L->v_base, bytes);
+        if (e != cudaSuccess) {
+            cudaFree(L->k_base);
+            L->k_base = L->v_base = nullptr;
+            return cuda_fail(e, "KV pool allocation");
+        }
+        L->owns_regions = true;
+    }
+    int st = gkv_table_create(m->device, max_blocks, &L->table);
+    if (st) {
+        release_layer(*L);
+        return st;
+    }
+    L->max_blocks = max_blocks;
+    L->k_pool.init(max_blocks);
+    L->v_pool.init(max_blocks);
+    L->k_ids.clear();
+    L->v_ids.clear();
+    L->on_device = 0;
+    L->num_cached = 0;
+    L->reserved = true;
+    return GKV_OK;
+}
+
+int gkv_is_active(const gkv_manager* m, int32_t layer_id) {
+    const Layer* L = find_layer(m, layer_id);
+    return L && L->active ? 1 : 0;
+}
+
+int gkv_append_kv_pages(gkv_manager* m, int32_t layer_id, int32_t count) {
+    Layer* L = nullptr;
+    int st = active_layer(m, layer_id, &L);
+    if (st) return st;
+    if (count <= 0) return GKV_OK;  // the reference ignores count <= 0 (:143)
+    int32_t first = 0, n = 0;
+    if ((st = grow(*L, count, &first, &n))) return st;
+    L->num_cached += count;
+    return GKV_OK;
+}
+
+int gkv_append_kv(gkv_manager* m, int32_t layer_id, const void* K, const void* V, int32_t n_kv_heads,
+                  int32_t seq_len, int32_t head_dim, int32_t dtype, gkv_stream_t stream) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    if (n_kv_heads != L->n_kv_heads || head_dim != L->head_dim || dtype != L->dtype)
+        return fail(GKV_ERR_INVALID, "K/V geometry does not match layer %d", layer_id);
+    if (seq_len <= 0) return GKV_OK;  // the reference returns early (:110)
+    int32_t first = 0, n = 0;
+    if ((st = grow(*L, seq_len, &first, &n))) return st;
+    gkv_pool_desc pool = pool_of(*L);
+    gkv_new_pages np = pending(*L);
+    st = gkv_append_kv_raw(&pool, L->table, L->num_cached, &np, K, V, seq_len, stream);
+    if (st) {
+        ungrow(*L, first);
+        return st;
+    }
+    L->on_device = static_cast<int32_t>(L->k_ids.size());
+    L->num_cached += seq_len;
+    return GKV_OK;
+}
+
+int gkv_paged_attention(gkv_manager* m, int32_t layer_id, const void* Q, const void* K, const void* V,
+                        void* out, int32_t batch, int32_t n_q_heads, int32_t seq_len, int32_t head_dim,
+                        int32_t n_kv_heads, float scale, int32_t causal, int32_t n_kv_groups,
+                        int32_t dtype, int32_t out_dtype, gkv_stream_t stream) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    if (batch != 1) return fail(GKV_ERR_UNSUPPORTED, "batch %d: the paged cache holds one sequence", batch);
+    if (n_kv_heads != L->n_kv_heads || head_dim != L->head_dim || dtype != L->dtype)
+        return fail(GKV_ERR_INVALID, "Q/K/V geometry does not match layer %d", layer_id);
+    if (n_kv_groups * n_kv_heads != n_q_heads)
+        return fail(GKV_ERR_INVALID, "n_kv_groups %d * n_kv_heads %d != n_q_heads %d", n_kv_groups, n_kv_heads,
+                    n_q_heads);
+    if (seq_len < 1) return fail(GKV_ERR_INVALID, "seq_len %d", seq_len);
+    int32_t first = 0, n = 0;
+    if ((st = grow(*L, seq_len, &first, &n))) return st;
+    gkv_pool_desc pool = pool_of(*L);
+    gkv_new_pages np = pending(*L);
+    st = gkv_paged_attention_raw(&pool, L->table, L->num_cached, &np, Q, K, V, out, n_q_heads, seq_len, scale,
+                                 causal, out_dtype, stream);
+    if (st) {
+        ungrow(*L, first);
+        return st;
+    }
+    L->on_device = static_cast<int32_t>(L->k_ids.size());
+    L->num_cached += seq_len;
+    return GKV_OK;
+}
+
+int gkv_reset_layer(gkv_manager* m, int32_t layer_id) {
+    Layer* L = find_layer(m, layer_id);
+    if (!L) return fail(GKV_ERR_STATE, "layer %d unknown", layer_id);
+    L->num_cached = 0;
+    L->k_ids.clear();
+    L->v_ids.clear();
+    L->on_device = 0;
+    L->k_pool.reset();
+    L->v_pool.reset();
+    return GKV_OK;
+}
+
+int gkv_reset(gkv_manager* m) {
+    if (!m) return fail(GKV_ERR_INVALID, "null manager");
+    for (auto& kv : m->layers) gkv_reset_layer(m, kv.first);
+    return GKV_OK;
+}
+
+int gkv_get_layer_info(const gkv_manager* m, int32_t layer_id, gkv_layer_info* info) {
+    const Layer* L = find_layer(m, layer_id);
+    if (!info) return fail(GKV_ERR_INVALID, "null info");
+    std::memset(info, 0, sizeof *info);
+    if (!L) return fail(GKV_ERR_STATE, "layer %d unknown", layer_id);
+    info->active = L->active;
+    info->num_cached = L->num_cached;
+    info->n_pages = static_cast<int32_t>(L->k_ids.size());
+    info->max_blocks = L->max_blocks;
+    info->n_kv_heads = L->n_kv_heads;
+    info->head_dim = L->head_dim;
+    info->dtype = L->dtype;
+    info->k_base = L->k_base;
+    info->v_base = L->v_base;
+    info->device_table = gkv_table_device_ptr(L->table);
+    return GKV_OK;
+}
+
+int gkv_get_page_table(const gkv_manager* m, int32_t layer_id, int32_t* k_ids, int32_t* v_ids, int32_t cap,
+                       int32_t* n_pages) {
+    const Layer* L = find_layer(m, layer_id);
+    if (!L) return fail(GKV_ERR_STATE, "layer %d unknown", layer_id);
+    const int32_t n = static_cast<int32_t>(L->k_ids.size());
+    if (n_pages) *n_pages = n;
+    for (int32_t i = 0; i < n && i < cap; ++i) {
+        if (k_ids) k_ids[i] = L->k_ids[i];
+        if (v_ids) v_ids[i] = L->v_ids[i];
+    }
+    return GKV_OK;
+}
+
+int gkv_read_device_table(gkv_manager* m, int32_t layer_id, int32_t* k_ids, int32_t* v_ids, int32_t cap,
+                          int32_t* n_published) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    const int32_t n = L->on_device;
+    if (n_published) *n_published = n;
+    const int32_t c = std::min(n, cap);
+    if (c <= 0) return GKV_OK;
+    DeviceGuard g(m->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "synchronise");
+    std::vector<int2> buf(c);
+    if ((e = cudaMemcpy(buf.data(), L->table->d_table, sizeof(int2) * c, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "table download");
+    for (int32_t i = 0; i < c; ++i) {
+        if (k_ids) k_ids[i] = buf[i].x;
+        if (v_ids) v_ids[i] = buf[i].y;
+    }
+    return GKV_OK;
+}
+
+int gkv_set_page_table(gkv_manager* m, int32_t layer_id, const int32_t* k_ids, const int32_t* v_ids,
+                       int32_t n_pages, int32_t num_cached, gkv_stream_t stream) {
+    Layer* L = nullptr;
+    int st = active_layer(m, layer_id, &L);
+    if (st) return st;
+    if (!L->reserved) return fail(GKV_ERR_STATE, "layer %d has no pools", layer_id);
+    if (n_pages < 0 || n_pages > L->max_blocks || (n_pages && (!k_ids || !v_ids)) || num_cached < 0 ||
+        num_cached > n_pages * 16 || (num_cached + 15) / 16 != n_pages)
+        return fail(GKV_ERR_INVALID, "table of %d pages cannot hold %d tokens", n_pages, num_cached);
+    for (int32_t i = 0; i < n_pages; ++i)
+        if (!L->k_pool.is_handed_out(k_ids[i]) || !L->v_pool.is_handed_out(v_ids[i]))
+            return fail(GKV_ERR_INVALID, "entry %d names a page the pool has not handed out", i);
+    std::vector<int2> dev(n_pages);
+    for (int32_t i = 0; i < n_pages; ++i) dev[i] = make_int2(k_ids[i], v_ids[i]);
+    DeviceGuard g(m->device >= 0 ? m->device : 0);
+    if (n_pages && L->table) {
+        // Pageable source: the copy is staged before this call returns.
+        cudaError_t e = cudaMemcpyAsync(L->table->d_table, dev.data(), sizeof(int2) * n_pages,
+                                        cudaMemcpyHostToDevice, reinterpret_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "table upload");
+    }
+    L->k_ids.assign(k_ids, k_ids + n_pages);
+    L->v_ids.assign(v_ids, v_ids + n_pages);
+    L->on_device = n_pages;
+    L->num_cached = num_cached;
+    return GKV_OK;
+}
+
+int gkv_page_alloc(gkv_manager* m, int32_t layer_id, int32_t which, int32_t* id) {
+    Layer* L = nullptr;
+    int st = active_layer(m, layer_id, &L);
+    if (st) return st;
+    if (!id || (which != 0 && which != 1)) return fail(GKV_ERR_INVALID, "bad arguments");
+    *id = (which == 0 ? L->k_pool : L->v_pool).alloc();
+    return *id < 0 ? fail(GKV_ERR_NO_PAGES, "pool exhausted") : GKV_OK;
+}
+
+int gkv_page_free(gkv_manager* m, int32_t layer_id, int32_t which, int32_t id) {
+    Layer* L = nullptr;
+    int st = active_layer(m, layer_id, &L);
+    if (st) return st;
+    if (which != 0 && which != 1) return fail(GKV_ERR_INVALID, "bad pool selector");
+    if ((which == 0 ? L->k_pool : L->v_pool).free(id) != 0)
+        return fail(GKV_ERR_INVALID, "page %d freed twice", id);
+    return GKV_OK;
+}
+
+int gkv_pool_reset(gkv_manager* m, int32_t layer_id, int32_t which) {
+    Layer* L = nullptr;
+    int st = active_layer(m, layer_id, &L);
+    if (st) return st;
+    if (which != 0 && which != 1) return fail(GKV_ERR_INVALID, "bad pool selector");
+    (which == 0 ? L->k_pool : L->v_pool).reset();
+    return GKV_OK;
+}
+
+int gkv_pool_stats(const gkv_manager* m, int32_t layer_id, int32_t which, int32_t* num_blocks, int32_t* num_free,
+                   int32_t* capacity) {
+    const Layer* L = find_layer(m, layer_id);
+    if (!L || !L->active) return fail(GKV_ERR_STATE, "layer %d is not initialised", layer_id);
+    if (which != 0 && which != 1) return fail(GKV_ERR_INVALID, "bad pool selector");
+    const PagePool& p = which == 0 ? L->k_pool : L->v_pool;
+    if (num_blocks) *num_blocks = p.num_blocks();
+    if (num_free) *num_free = p.num_free();
+    if (capacity) *capacity = p.capacity();
+    return GKV_OK;
+}
+
+int gkv_check_device_errors(gkv_manager* m, int32_t layer_id, uint32_t* flags) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    return gkv_table_check_errors(L->table, flags);
+}
+
+}  // extern "C"

@@ -1,0 +1,91 @@
+// kernels.h — internal launch interface between the host runtime (host.cpp)
+// and the CUDA kernels. Not part of the C ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gkv {
+
+constexpr int kPageSlots = 16;  // PAGE_BLOCK_SIZE (include/core/page_attention.h:9)
+constexpr int kHeadDim = 128;   // the reference CUDA op's only head size (attention.cu:511)
+
+// Table entries a launch publishes to the device block table. The kernels
+// read entries [first, first + n) from here (not from the table, which they
+// are writing) and one thread stores them into the table.
+constexpr int kMaxNewPagesPerLaunch = 64;
+struct NewPages {
+    int32_t first;
+    int32_t n;
+    int2 ids[kMaxNewPagesPerLaunch];  // {k_id, v_id}
+};
+
+// Split-K partials capacity (q-head rows x splits) of one scratch area.
+constexpr int kMaxPartialRows = 4096;
+
+struct Scratch {
+    float* part_acc;     // [kMaxPartialRows][128] un-normalised outputs
+    float2* part_ml;     // [kMaxPartialRows] (running max in log2 units, sum)
+    uint32_t* counters;  // [n_kv_heads] split completion tickets, zero between launches
+    uint32_t* err;       // device error word
+    int32_t counters_len;
+};
+
+struct PoolView {
+    uint16_t* k_base;
+    uint16_t* v_base;
+    int32_t pool_pages;
+    int32_t n_kv_heads;
+};
+
+// Encode the 3-D tensor maps (D, Hkv, pool_pages*16) over a K or V pool.
+bool encode_pool_maps(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map,
+                      const char** why);
+
+struct DecodeLaunch {
+    const uint16_t* q;      // [Hq][128]
+    const uint16_t* k_new;  // [Hkv][128] token appended by this step (or null)
+    const uint16_t* v_new;
+    void* out;              // [Hq][128]
+    int32_t out_dtype;
+    int32_t n_q_heads;
+    int32_t n_prior;        // tokens cached before this step
+    int32_t total;          // tokens attended (n_prior + 1 with an append)
+    int32_t n_pages;        // logical pages covering `total`
+    float scale;
+    int32_t n_splits;       // 0 = choose
+};
+
+// Fused decode step: append one token's K/V, GQA-grouped split-K
+// flash-decoding over the block table, split combine. Returns the CUDA error.
+cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map,
+                          int2* table, const NewPages& np, const Scratch& scratch,
+                          const DecodeLaunch& d, int num_sms, cudaStream_t stream);
+
+// Scatter tokens [p_begin, p_end) of K/V ([Hkv][src_len][128]) to positions
+// n_prior + p, and publish np's entries to the table. With p_begin == p_end
+// only the table entries are written.
+cudaError_t launch_append(const PoolView& pool, int2* table, const NewPages& np,
+                          const uint16_t* k, const uint16_t* v, int32_t n_prior,
+                          int32_t src_len, int32_t p_begin, int32_t p_end, uint32_t* err,
+                          cudaStream_t stream);
+
+struct PrefillLaunch {
+    const uint16_t* q;  // [Hq][S][128]
+    void* out;          // [Hq][S][128]
+    int32_t out_dtype;
+    int32_t n_q_heads;
+    int32_t seq_len;
+    int32_t total;      // tokens cached including this chunk
+    int32_t n_pages;
+    float scale;
+    int32_t causal;
+};
+
+// Attention of a chunk of seq_len queries over the cached pages (the chunk's
+// own K/V already appended).
+cudaError_t launch_prefill(const PoolView& pool, const CUtensorMap& k_map,
+                           const CUtensorMap& v_map, const int2* table, const PrefillLaunch& p,
+                           uint32_t* err, int num_sms, cudaStream_t stream);
+
+}  // namespace gkv

@@ -1,0 +1,259 @@
+"""Python mirror of Genllm's paged-attention operator interface, on the C ABI.
+
+Names, argument meaning and error behaviour follow the reference (paths
+relative to the Genllm source tree):
+
+* :class:`PagedAttentionManager` — ``PagedAttentionManager``
+  (include/core/page_attention.h:52-89): ``init_layer``, ``reserve_layer``,
+  ``append_kv_from_tensor``, ``append_kv_pages``, ``reset``, ``is_active``,
+  ``get_layer``; the layer's K/V ``BlockPool`` s (page_attention.h:11-45) are
+  reached through :meth:`PagedAttentionManager.pool`.
+* :func:`paged_attention` — ``kernel::paged_attention`` /
+  ``PagedAttentionImpl<Device::CUDA>::execute`` (include/core/kernels.h:32,
+  src/backend/cuda/attention.cu:491-580): append this step's K/V into the
+  layer's pages, then attend Q over the whole cache.
+
+torch supplies device memory and the current stream only; all the work runs
+in libgenllm_kv.so. Where the reference fails silently (inactive layer,
+exhausted pool) this raises :class:`GkvError`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+
+from . import _lib
+from ._lib import GKV_BF16, GKV_F16, GKV_F32, GkvError, check, lib
+
+PAGE_BLOCK_SIZE = 16
+
+_TORCH_TO_GKV = {torch.float32: GKV_F32, torch.float16: GKV_F16, torch.bfloat16: GKV_BF16}
+
+
+def _stream_handle(device: Optional[torch.device], stream=None):
+    if device is None:
+        return C.c_void_p(0)
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return C.c_void_p(s.cuda_stream)
+
+
+@dataclass
+class PageEntry:
+    """include/core/page_attention.h:47-50"""
+    k_block_id: int
+    v_block_id: int
+
+
+@dataclass
+class LayerState:
+    """Snapshot of include/core/page_attention.h:57-66 (LayerState)."""
+    active: bool
+    num_cached: int
+    n_kv_heads: int
+    head_dim: int
+    dtype: int
+    max_blocks: int
+    page_table: List[PageEntry] = field(default_factory=list)
+
+
+class BlockPoolView:
+    """The K (which=0) or V (which=1) BlockPool of one layer
+    (src/core/page_attention.cpp:25-64)."""
+
+    def __init__(self, mgr: "PagedAttentionManager", layer_id: int, which: int):
+        self._m, self._layer, self._which = mgr, layer_id, which
+
+    def alloc(self) -> int:
+        """LIFO id, or -1 when exhausted (the reference's contract)."""
+        out = C.c_int32(-1)
+        st = lib().gkv_page_alloc(self._m.handle, self._layer, self._which, C.byref(out))
+        if st == _lib.GKV_ERR_NO_PAGES:
+            return -1
+        check(st)
+        return out.value
+
+    def free(self, block_id: int) -> None:
+        check(lib().gkv_page_free(self._m.handle, self._layer, self._which, int(block_id)))
+
+    def reset(self) -> None:
+        check(lib().gkv_pool_reset(self._m.handle, self._layer, self._which))
+
+    def _stats(self):
+        a, b, c = C.c_int32(), C.c_int32(), C.c_int32()
+        check(lib().gkv_pool_stats(self._m.handle, self._layer, self._which, C.byref(a), C.byref(b), C.byref(c)))
+        return a.value, b.value, c.value
+
+    def num_blocks(self) -> int:
+        return self._stats()[0]
+
+    def num_free(self) -> int:
+        return self._stats()[1]
+
+    def capacity(self) -> int:
+        return self._stats()[2]
+
+    def empty(self) -> bool:
+        return self.num_blocks() == 0
+
+
+class PagedAttentionManager:
+    """Per-device paged KV-cache manager (include/core/page_attention.h:52-89)."""
+
+    def __init__(self, device: int | torch.device = 0):
+        """``device=-1`` gives a host-only manager (page bookkeeping, no device
+        memory), the counterpart of the reference's pool-less manager."""
+        if isinstance(device, int) and device == -1:
+            self.device = None
+        else:
+            dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+            if dev.type != "cuda":
+                raise ValueError("the paged KV cache lives on a CUDA device")
+            self.device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+        h = C.c_void_p()
+        check(lib().gkv_manager_create(-1 if self.device is None else self.device.index, C.byref(h)))
+        self.handle = h
+        self._regions = {}  # layer -> (k_pool tensor, v_pool tensor)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().gkv_manager_destroy(self.handle)
+            self.handle = None
+            self._regions.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- page_attention.cpp:72-101 -------------------------------------
+    def init_layer(self, layer_id: int, n_kv_heads: int, head_dim: int, dtype: int = GKV_BF16) -> None:
+        check(lib().gkv_init_layer(self.handle, layer_id, n_kv_heads, head_dim, dtype))
+
+    def reserve_layer(self, layer_id: int, max_blocks: int,
+                      k_region: Optional[torch.Tensor] = None, v_region: Optional[torch.Tensor] = None) -> None:
+        """Give the layer K and V pools of max_blocks pages. Without regions the
+        pools are torch allocations owned by this manager (exposed by
+        :meth:`pool_tensors`); with regions they are caller memory."""
+        info = self._info(layer_id)
+        if self.device is None:
+            check(lib().gkv_reserve_layer(self.handle, layer_id, max_blocks, None, None))
+            return
+        if k_region is None:
+            shape = (max_blocks, PAGE_BLOCK_SIZE, info.n_kv_heads, info.head_dim)
+            td = {GKV_BF16: torch.bfloat16, GKV_F16: torch.float16, GKV_F32: torch.float32}[info.dtype]
+            k_region = torch.empty(shape, dtype=td, device=self.device)
+            v_region = torch.empty(shape, dtype=td, device=self.device)
+        check(lib().gkv_reserve_layer(self.handle, layer_id, max_blocks, C.c_void_p(k_region.data_ptr()),
+                                      C.c_void_p(v_region.data_ptr())))
+        self._regions[layer_id] = (k_region, v_region)
+
+    def is_active(self, layer_id: int) -> bool:
+        return bool(lib().gkv_is_active(self.handle, layer_id))
+
+    # -- page_attention.cpp:104-162 -------------------------------------
+    def append_kv_pages(self, layer_id: int, count: int) -> None:
+        check(lib().gkv_append_kv_pages(self.handle, layer_id, count))
+
+    def append_kv_from_tensor(self, layer_id: int, K: torch.Tensor, V: torch.Tensor, stream=None) -> None:
+        """K, V: [1, Hkv, S, D] (or [Hkv, S, D]) contiguous on this device."""
+        Kc, Vc = _kv_view(K), _kv_view(V)
+        hkv, s, d = Kc.shape
+        check(lib().gkv_append_kv(self.handle, layer_id, C.c_void_p(Kc.data_ptr()), C.c_void_p(Vc.data_ptr()),
+                                  hkv, s, d, _TORCH_TO_GKV[Kc.dtype], _stream_handle(self.device, stream)))
+
+    # -- page_attention.cpp:205-216 -------------------------------------
+    def reset(self) -> None:
+        check(lib().gkv_reset(self.handle))
+
+    def reset_layer(self, layer_id: int) -> None:
+        check(lib().gkv_reset_layer(self.handle, layer_id))
+
+    def get_layer(self, layer_id: int) -> LayerState:
+        info = self._info(layer_id)
+        k, v = self.page_table(layer_id)
+        return LayerState(bool(info.active), info.num_cached, info.n_kv_heads, info.head_dim, info.dtype,
+                          info.max_blocks, [PageEntry(int(a), int(b)) for a, b in zip(k, v)])
+
+    def pool(self, layer_id: int, which: int) -> BlockPoolView:
+        return BlockPoolView(self, layer_id, which)
+
+    def pool_tensors(self, layer_id: int):
+        """(K pool, V pool) tensors [max_blocks][16][Hkv][D] of the layer."""
+        return self._regions[layer_id]
+
+    def page_table(self, layer_id: int):
+        n = C.c_int32()
+        check(lib().gkv_get_page_table(self.handle, layer_id, None, None, 0, C.byref(n)))
+        k = (C.c_int32 * max(n.value, 1))()
+        v = (C.c_int32 * max(n.value, 1))()
+        check(lib().gkv_get_page_table(self.handle, layer_id, k, v, n.value, C.byref(n)))
+        return list(k)[: n.value], list(v)[: n.value]
+
+    def set_page_table(self, layer_id: int, k_ids, v_ids, num_cached: int, stream=None) -> None:
+        n = len(k_ids)
+        ka = (C.c_int32 * max(n, 1))(*[int(x) for x in k_ids])
+        va = (C.c_int32 * max(n, 1))(*[int(x) for x in v_ids])
+        check(lib().gkv_set_page_table(self.handle, layer_id, ka, va, n, num_cached,
+                                       _stream_handle(self.device, stream)))
+
+    def device_table(self, layer_id: int):
+        """The device copy of the block table (synchronises): (k_ids, v_ids)."""
+        n = C.c_int32()
+        check(lib().gkv_read_device_table(self.handle, layer_id, None, None, 0, C.byref(n)))
+        k = (C.c_int32 * max(n.value, 1))()
+        v = (C.c_int32 * max(n.value, 1))()
+        check(lib().gkv_read_device_table(self.handle, layer_id, k, v, n.value, C.byref(n)))
+        return list(k)[: n.value], list(v)[: n.value]
+
+    def check_device_errors(self, layer_id: int) -> int:
+        f = C.c_uint32()
+        check(lib().gkv_check_device_errors(self.handle, layer_id, C.byref(f)))
+        return f.value
+
+    def _info(self, layer_id: int) -> _lib.LayerInfo:
+        info = _lib.LayerInfo()
+        check(lib().gkv_get_layer_info(self.handle, layer_id, C.byref(info)))
+        return info
+
+
+def _kv_view(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise GkvError(_lib.GKV_ERR_UNSUPPORTED, "batch must be 1")
+        t = t[0]
+    if t.dim() != 3 or not t.is_contiguous():
+        raise GkvError(_lib.GKV_ERR_INVALID, "expected a contiguous [1, H, S, D] tensor")
+    return t
+
+
+def paged_attention(manager: PagedAttentionManager, layer_id: int, Q: torch.Tensor, K: torch.Tensor,
+                    V: torch.Tensor, out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                    causal: bool = True, num_kv_groups: Optional[int] = None, stream=None) -> torch.Tensor:
+    """``PagedAttentionImpl<CUDA>::execute`` on torch tensors.
+
+    Q: [1, Hq, S, D]; K, V: [1, Hkv, S, D] (post-RoPE, post-QK-norm); out
+    (optional, preallocated like the reference's activation-pool output):
+    [1, Hq, S, D] in any of f32/f16/bf16 — Q's dtype by default, as the
+    reference. ``scale`` defaults to 1/sqrt(D) (op_params[1]), ``causal`` is
+    op_params[2], ``num_kv_groups`` = Hq / Hkv (op_params[3]).
+    """
+    if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
+        raise GkvError(_lib.GKV_ERR_INVALID, "Q, K, V must be [B, H, S, D]")
+    B, Hq, S, D = Q.shape
+    Hkv = K.shape[1]
+    if out is None:
+        out = torch.empty_like(Q)
+    groups = num_kv_groups if num_kv_groups is not None else Hq // Hkv
+    sc = float(scale) if scale is not None else 1.0 / float(D) ** 0.5
+    for t in (Q, K, V, out):
+        if not t.is_contiguous() or t.device != manager.device:
+            raise GkvError(_lib.GKV_ERR_INVALID, "tensors must be contiguous and on the manager's device")
+    check(lib().gkv_paged_attention(manager.handle, layer_id, C.c_void_p(Q.data_ptr()), C.c_void_p(K.data_ptr()),
+                                    C.c_void_p(V.data_ptr()), C.c_void_p(out.data_ptr()), B, Hq, S, D, Hkv, sc,
+                                    1 if causal else 0, groups, _TORCH_TO_GKV[Q.dtype], _TORCH_TO_GKV[out.dtype],
+                                    _stream_handle(manager.device, stream)))
+    return out

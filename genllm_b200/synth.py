@@ -1,0 +1,118 @@
+"""Seeded synthetic workloads for the paged KV-cache path.
+
+The reference ships no dataset or benchmark inputs for this path; every
+config is synthetic (bf16 N(0,1) values, seeded fragmented block tables).
+Both the parity tests and bench.py build their inputs here so that the CUDA
+path and the CPU checkers see identical bytes.
+
+A *fragmented case* reproduces a cache that has been filled and partly
+recycled: every physical page of a ``pool_pages`` pool is handed out, the
+ones not in the table are returned to the free list, and the table is a
+seeded permutation. The K and V pools use independent permutations (the
+reference keeps separate K and V id streams, PageEntry{k_block_id,
+v_block_id}, include/core/page_attention.h:47-50).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+PAGE_SLOTS = 16  # PAGE_BLOCK_SIZE, include/core/page_attention.h:9
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bits, round to nearest even, exponent-0 inputs flushed to
+    signed zero (the reference's conversion, include/utils/bfloat16.hpp:18-41)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    sign = u >> 31
+    e = (u >> 23) & 0xFF
+    m = u & 0x7FFFFF
+    low = u & 0xFFFF
+    up = ((low > 0x8000) | ((low == 0x8000) & ((m & 0x10000) != 0))).astype(np.uint32)
+    hm = (m >> 16) + up
+    carry = hm >= 0x80
+    e2 = e + carry.astype(np.uint32)
+    hm = np.where(carry, 0, hm)
+    out = (sign << 15) | (e2 << 7) | hm
+    out = np.where(e2 >= 0xFF, (sign << 15) | 0x7F80, out)
+    out = np.where(e == 0, sign << 15, out)
+    out = np.where(e == 0xFF, (sign << 15) | 0x7F80 | (m != 0).astype(np.uint32), out)
+    return out.astype(np.uint16)
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def randn_bf16(rng: np.random.Generator, shape) -> np.ndarray:
+    return bf16_bits(rng.standard_normal(shape, dtype=np.float32))
+
+
+@dataclass
+class FragmentedCase:
+    n_q_heads: int
+    n_kv_heads: int
+    head_dim: int
+    n_prior: int           # tokens already in the cache
+    n_new: int             # tokens appended by the step (1 = decode)
+    pool_pages: int
+    k_ids: np.ndarray      # int32 [ceil(n_prior/16)] physical K page per logical page
+    v_ids: np.ndarray
+    k_free_order: np.ndarray  # ids returned to the K free list, in order
+    v_free_order: np.ndarray
+    k_pool: np.ndarray     # uint16 [pool_pages][16][Hkv][D]
+    v_pool: np.ndarray
+    q: np.ndarray          # uint16 [Hq][S][D]
+    k_new: np.ndarray      # uint16 [Hkv][S][D]
+    v_new: np.ndarray
+    scale: float
+
+    @property
+    def n_pages(self) -> int:
+        return len(self.k_ids)
+
+    @property
+    def total(self) -> int:
+        return self.n_prior + self.n_new
+
+
+def fragmented_case(seed: int, n_q_heads: int, n_kv_heads: int, head_dim: int, n_prior: int,
+                    pool_pages: int, n_new: int = 1, fill_pools: bool = True,
+                    poison_unused: bool = False) -> FragmentedCase:
+    """Build the inputs of one paged-attention step.
+
+    Config 1 of the path (Qwen3-0.6B layer): ``fragmented_case(0, 16, 8, 128,
+    1024, 256)``. With ``poison_unused`` the slots no table entry covers hold
+    NaN bit patterns, so a kernel that reads past the valid tokens shows up.
+    """
+    rng = np.random.default_rng(seed)
+    n_pages = (n_prior + PAGE_SLOTS - 1) // PAGE_SLOTS
+    if n_pages > pool_pages:
+        raise ValueError("pool too small for the prior tokens")
+    kp = rng.permutation(pool_pages).astype(np.int32)
+    vp = rng.permutation(pool_pages).astype(np.int32)
+    shape = (pool_pages, PAGE_SLOTS, n_kv_heads, head_dim)
+    if fill_pools:
+        k_pool = randn_bf16(rng, shape)
+        v_pool = randn_bf16(rng, shape)
+        if poison_unused:
+            nan = np.uint16(0x7FC1)
+            used_k = np.zeros(pool_pages, bool); used_k[kp[:n_pages]] = True
+            used_v = np.zeros(pool_pages, bool); used_v[vp[:n_pages]] = True
+            k_pool[~used_k] = nan
+            v_pool[~used_v] = nan
+            tail = n_prior - (n_pages - 1) * PAGE_SLOTS if n_pages else PAGE_SLOTS
+            if n_pages and tail < PAGE_SLOTS:
+                k_pool[kp[n_pages - 1], tail:] = nan
+                v_pool[vp[n_pages - 1], tail:] = nan
+    else:
+        k_pool = np.zeros(0, np.uint16)
+        v_pool = np.zeros(0, np.uint16)
+    q = randn_bf16(rng, (n_q_heads, n_new, head_dim))
+    k_new = randn_bf16(rng, (n_kv_heads, n_new, head_dim))
+    v_new = randn_bf16(rng, (n_kv_heads, n_new, head_dim))
+    return FragmentedCase(n_q_heads, n_kv_heads, head_dim, n_prior, n_new, pool_pages,
+                          kp[:n_pages].copy(), vp[:n_pages].copy(), kp[n_pages:].copy(),
+                          vp[n_pages:].copy(), k_pool, v_pool, q, k_new, v_new,
+                          float(1.0 / np.sqrt(head_dim)))

@@ -1,0 +1,114 @@
+"""Device-resident decode workload of the paged KV-cache path (bench config 3/5).
+
+Builds ``n_layers`` layers of Qwen3-4B attention shape (Hq=32, Hkv=8, D=128,
+bf16) on one GPU, each holding ``ctx`` cached tokens in a fragmented block
+table: all pages of a ``pool_pages`` pool handed out, the unused ones freed
+(seeded order), the table a seeded permutation. Values are N(0,1) bf16 drawn
+on the device (seeded). With ``world``/``rank`` the KV heads are sharded: the
+rank owns kv heads [rank*Hkv/world, (rank+1)*Hkv/world) and the matching
+query heads, while the page ids (and so the block table) are identical on
+every rank.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .paged_attention import PagedAttentionManager
+
+PAGE = 16
+
+
+def shard_heads(n_q_heads: int, n_kv_heads: int, world: int, rank: int):
+    """(q_head_begin, q_head_end, kv_head_begin, kv_head_end) of one rank."""
+    if n_kv_heads % world:
+        raise ValueError(f"{n_kv_heads} kv heads do not split over {world} ranks")
+    g = n_q_heads // n_kv_heads
+    hk = n_kv_heads // world
+    return rank * hk * g, (rank + 1) * hk * g, rank * hk, (rank + 1) * hk
+
+
+@dataclass
+class LayerBufs:
+    q: torch.Tensor      # [1, Hq_local, 1, D] bf16
+    k: torch.Tensor      # [1, Hkv_local, 1, D]
+    v: torch.Tensor
+    out: torch.Tensor    # [1, Hq_local, 1, D] bf16
+
+
+class DecodeWorkload:
+    def __init__(self, device: int, n_layers=36, ctx=32768, pool_pages=4096, n_q_heads=32, n_kv_heads=8,
+                 head_dim=128, seed=0, world=1, rank=0):
+        self.device = torch.device("cuda", device)
+        self.n_layers, self.ctx, self.pool_pages = n_layers, ctx, pool_pages
+        self.Hq, self.Hkv, self.D = n_q_heads, n_kv_heads, head_dim
+        qb, qe, kb, ke = shard_heads(n_q_heads, n_kv_heads, world, rank)
+        self.hq_local, self.hkv_local = qe - qb, ke - kb
+        self.scale = 1.0 / float(head_dim) ** 0.5
+        self.mgr = PagedAttentionManager(device)
+        self.layers = []
+        n_pages = (ctx + PAGE - 1) // PAGE
+        for l in range(n_layers):
+            rng = np.random.default_rng(seed * 1000 + l)
+            kperm = rng.permutation(pool_pages).astype(np.int32)
+            vperm = rng.permutation(pool_pages).astype(np.int32)
+            self.mgr.init_layer(l, self.hkv_local, head_dim)
+            self.mgr.reserve_layer(l, pool_pages)
+            kp, vp = self.mgr.pool_tensors(l)
+            g = torch.Generator(device=self.device)
+            # Full-head values drawn per layer, then this rank's heads kept, so
+            # that every sharding sees the same cache contents.
+            for t, off in ((kp, 1), (vp, 2)):
+                g.manual_seed(seed * 1000003 + l * 7 + off)
+                for p0 in range(0, pool_pages, 512):
+                    p1 = min(pool_pages, p0 + 512)
+                    full = torch.randn((p1 - p0, PAGE, n_kv_heads, head_dim), generator=g, device=self.device)
+                    t[p0:p1].copy_(full[:, :, kb:ke].to(torch.bfloat16))
+            for w, perm in ((0, kperm), (1, vperm)):
+                lib = _lib.lib()
+                out = C.c_int32()
+                for _ in range(pool_pages):
+                    _lib.check(lib.gkv_page_alloc(self.mgr.handle, l, w, C.byref(out)))
+                for pid in perm[n_pages:]:
+                    _lib.check(lib.gkv_page_free(self.mgr.handle, l, w, int(pid)))
+            self.mgr.set_page_table(l, kperm[:n_pages], vperm[:n_pages], ctx)
+            g.manual_seed(seed * 1000003 + l * 7 + 3)
+            q = torch.randn((1, n_q_heads, 1, head_dim), generator=g, device=self.device)[:, qb:qe].to(torch.bfloat16)
+            k = torch.randn((1, n_kv_heads, 1, head_dim), generator=g, device=self.device)[:, kb:ke].to(torch.bfloat16)
+            v = torch.randn((1, n_kv_heads, 1, head_dim), generator=g, device=self.device)[:, kb:ke].to(torch.bfloat16)
+            out_t = torch.empty((1, self.hq_local, 1, head_dim), dtype=torch.bfloat16, device=self.device)
+            self.layers.append(LayerBufs(q.contiguous(), k.contiguous(), v.contiguous(), out_t))
+        torch.cuda.synchronize(self.device)
+        self._fn = _lib.lib().gkv_paged_attention
+        self._args = [
+            (self.mgr.handle, l, C.c_void_p(b.q.data_ptr()), C.c_void_p(b.k.data_ptr()), C.c_void_p(b.v.data_ptr()),
+             C.c_void_p(b.out.data_ptr()), 1, self.hq_local, 1, head_dim, self.hkv_local, C.c_float(self.scale), 1,
+             self.hq_local // self.hkv_local, _lib.GKV_BF16, _lib.GKV_BF16)
+            for l, b in enumerate(self.layers)]
+
+    def cached(self, layer: int = 0) -> int:
+        return self.mgr.get_layer(layer).num_cached
+
+    def layer_step(self, l: int, stream_handle) -> None:
+        """One decode step of layer l through the C ABI (append + attention)."""
+        st = self._fn(*self._args[l], stream_handle)
+        if st:
+            _lib.check(st)
+
+    def bytes_per_layer_token(self, total_tokens: int) -> int:
+        """Algorithmic HBM bytes of one fused decode launch attending
+        total_tokens tokens (the new one included): every K and V row read
+        once, Q read, the bf16 output written, the new K/V row read from the
+        input and written to its page, the block table read."""
+        row = self.hkv_local * self.D * 2
+        n_pages = (total_tokens + PAGE - 1) // PAGE
+        kv_read = 2 * (total_tokens - 1) * row
+        new_kv = 2 * 2 * row
+        q = self.hq_local * self.D * 2
+        out = self.hq_local * self.D * 2
+        table = n_pages * 8
+        return kv_read + new_kv + q + out + table

@@ -1,0 +1,235 @@
+/*
+ * genllm_kv.h — C ABI of the B200-native paged KV-cache path.
+ *
+ * Replaces the CUDA side of Genllm's paged-attention path (paths relative to
+ * the Genllm source tree):
+ *   - BlockPool / PagedAttentionManager   include/core/page_attention.h:11-89,
+ *                                         src/core/page_attention.cpp:25-216
+ *   - PagedAttentionImpl<Device::CUDA>    include/backend/cuda/attention.h:16-18,
+ *                                         src/backend/cuda/attention.cu:491-580
+ *   - kernel::paged_attention             include/core/kernels.h:32
+ *
+ * Two tiers:
+ *   1. the managed tier (gkv_manager_*, gkv_*_layer, gkv_paged_attention ...)
+ *      mirrors PagedAttentionManager: it owns the per-layer LIFO page
+ *      allocators, the host copy of each block table and a device-resident
+ *      copy of it, and launches the kernels;
+ *   2. the raw tier (gkv_table_*, gkv_*_raw) runs the kernels over pools and
+ *      page allocation that the CALLER manages (e.g. the reference's own
+ *      BlockPool, when this library is dropped in under the unchanged
+ *      scheduler). The managed tier is built on the raw tier.
+ *
+ * Conventions: every function returns a gkv_status (0 = success); work is
+ * enqueued on the given cudaStream_t (0 = legacy default stream) and nothing
+ * synchronises unless documented. No function takes or returns torch types.
+ * Calls on one manager (or one gkv_table) must be ordered on one stream:
+ * they share split-K scratch and the device block table.
+ *
+ * Shapes follow the reference operator (include/model/op_factory.hpp:413-476):
+ * Q [1][Hq][S][D], K and V [1][Hkv][S][D], out [1][Hq][S][D], all contiguous;
+ * D = 128 (the reference CUDA op's requirement, attention.cu:511); page layout
+ * [16 slots][Hkv][D] (src/core/page_attention.cpp:128-129).
+ */
+#ifndef GENLLM_KV_H
+#define GENLLM_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without including the CUDA headers. */
+typedef struct CUstream_st* gkv_stream_t;
+
+#define GKV_PAGE_SLOTS 16 /* PAGE_BLOCK_SIZE, include/core/page_attention.h:9 */
+
+typedef enum gkv_status {
+    GKV_OK = 0,
+    GKV_ERR_INVALID = 1,     /* bad argument, unknown layer, shape mismatch */
+    GKV_ERR_NO_PAGES = 2,    /* a page pool is exhausted (the reference silently
+                                corrupts its table here, page_attention.cpp:155,161) */
+    GKV_ERR_CUDA = 3,        /* a CUDA runtime call failed; see gkv_last_error() */
+    GKV_ERR_UNSUPPORTED = 4, /* dtype / head_dim / batch / group size not built */
+    GKV_ERR_STATE = 5,       /* layer not initialised or not reserved */
+    GKV_ERR_DEVICE = 6       /* a kernel flagged an error (bad page id, wait timeout) */
+} gkv_status;
+
+/* Element types use the reference's DataType codes (include/utils/utils.hpp). */
+typedef enum gkv_dtype { GKV_F32 = 0, GKV_F16 = 1, GKV_BF16 = 30 } gkv_dtype;
+
+/* Status text, and the message of the last failure on this host thread. */
+const char* gkv_status_string(int status);
+const char* gkv_last_error(void);
+
+/* ======================= managed tier ==================================== */
+
+typedef struct gkv_manager gkv_manager;
+
+/* PagedAttentionManager(MemoryPool*) (page_attention.cpp:66-70) for CUDA
+ * device `device`. device = -1 makes a host-only manager: page bookkeeping
+ * (init/reserve/append_kv_pages/alloc/free/reset/tables) with no device memory
+ * and no CUDA calls, like the reference's pool-less manager used by its
+ * allocator tests (tests/test_page_attention.cpp:49-85); launches on it
+ * return GKV_ERR_STATE. Before reserve_layer a layer's pools are unbounded,
+ * as the reference's default BlockPool. */
+int gkv_manager_create(int device, gkv_manager** out);
+int gkv_manager_destroy(gkv_manager* m);
+
+/* init_layer (page_attention.cpp:72-79): mark the layer active with its KV
+ * geometry; resets its cached-token count. */
+int gkv_init_layer(gkv_manager* m, int32_t layer_id, int32_t n_kv_heads, int32_t head_dim,
+                   int32_t dtype);
+
+/* reserve_layer (page_attention.cpp:81-101): give the layer a K and a V region
+ * of max_blocks pages each. With k_region/v_region NULL the library allocates
+ * them (cudaMalloc, freed by gkv_manager_destroy); otherwise they are caller
+ * memory (e.g. carved from the reference's kv_cache MemoryPool), at least
+ * 16-byte aligned and max_blocks * 16 * Hkv * D * elem bytes long. Also
+ * allocates the layer's device block table. */
+int gkv_reserve_layer(gkv_manager* m, int32_t layer_id, int32_t max_blocks, void* k_region,
+                      void* v_region);
+
+/* is_active (page_attention.h:82-85): 1 active, 0 not. */
+int gkv_is_active(const gkv_manager* m, int32_t layer_id);
+
+/* append_kv_pages (page_attention.cpp:141-162): grow the table for `count`
+ * more tokens and advance num_cached, host bookkeeping only. Unlike the
+ * reference, when a pool cannot supply every page this returns
+ * GKV_ERR_NO_PAGES and changes nothing. The new table entries reach the
+ * device with the next append/attention launch on this layer. */
+int gkv_append_kv_pages(gkv_manager* m, int32_t layer_id, int32_t count);
+
+/* append_kv_from_tensor (page_attention.cpp:104-139): allocate pages, then
+ * scatter K and V ([Hkv][seq_len][D] device pointers) into them with one
+ * kernel. Bit-exact byte copy. */
+int gkv_append_kv(gkv_manager* m, int32_t layer_id, const void* K, const void* V,
+                  int32_t n_kv_heads, int32_t seq_len, int32_t head_dim, int32_t dtype,
+                  gkv_stream_t stream);
+
+/* PagedAttentionImpl<CUDA>::execute (attention.cu:491-580) / the CPU op
+ * (src/backend/cpu/attention.cpp:123-216): append this step's K/V, then attend
+ * Q over every cached token, causally when `causal` (query sq sits at absolute
+ * position num_cached - seq_len + sq). seq_len == 1 runs the fused split-K
+ * decode kernel (append + attention + split combine); seq_len > 1 runs the
+ * append kernel and the chunked-prefill kernel. Device pointers. `out_dtype`
+ * may differ from the K/V dtype (F32 output gives the pre-rounding values).
+ * n_kv_groups = Hq / Hkv (op_params[3]). batch must be 1 (the reference
+ * shares one cache across the batch; README.md:150 states batch 1). */
+int gkv_paged_attention(gkv_manager* m, int32_t layer_id, const void* Q, const void* K,
+                        const void* V, void* out, int32_t batch, int32_t n_q_heads,
+                        int32_t seq_len, int32_t head_dim, int32_t n_kv_heads, float scale,
+                        int32_t causal, int32_t n_kv_groups, int32_t dtype, int32_t out_dtype,
+                        gkv_stream_t stream);
+
+/* reset (page_attention.cpp:209-216) for every layer, or one layer. Host
+ * bookkeeping only: num_cached = 0, empty table, every page handed out so far
+ * back on the free list in ascending order. */
+int gkv_reset(gkv_manager* m);
+int gkv_reset_layer(gkv_manager* m, int32_t layer_id);
+
+typedef struct gkv_layer_info {
+    int32_t active;
+    int32_t num_cached;
+    int32_t n_pages;     /* logical pages in the table */
+    int32_t max_blocks;  /* pages per pool */
+    int32_t n_kv_heads;
+    int32_t head_dim;
+    int32_t dtype;
+    int32_t reserved;
+    void* k_base;        /* device address of page 0 of the K pool */
+    void* v_base;
+    const int32_t* device_table; /* [max_blocks][2] {k_id, v_id}, valid for n_pages
+                                    entries once the launches that wrote them ran */
+} gkv_layer_info;
+
+/* get_layer (page_attention.cpp:205-207), as a snapshot. */
+int gkv_get_layer_info(const gkv_manager* m, int32_t layer_id, gkv_layer_info* info);
+
+/* Copy the host block table (PageEntry list) into k_ids/v_ids (cap entries);
+ * *n_pages receives the full length. */
+int gkv_get_page_table(const gkv_manager* m, int32_t layer_id, int32_t* k_ids, int32_t* v_ids,
+                       int32_t cap, int32_t* n_pages);
+
+/* Synchronise the device and copy the DEVICE block table's first n_pages
+ * entries (those the launches so far have published) into k_ids/v_ids. A
+ * debugging and test aid: it must equal gkv_get_page_table after any
+ * append/attention launch. */
+int gkv_read_device_table(gkv_manager* m, int32_t layer_id, int32_t* k_ids, int32_t* v_ids,
+                          int32_t cap, int32_t* n_published);
+
+/* Replace the layer's table and num_cached (e.g. to restore a saved cache or
+ * to build a fragmented one in tests). Every id must already be handed out by
+ * the pool (gkv_page_alloc). Uploads the table on `stream`. */
+int gkv_set_page_table(gkv_manager* m, int32_t layer_id, const int32_t* k_ids,
+                       const int32_t* v_ids, int32_t n_pages, int32_t num_cached,
+                       gkv_stream_t stream);
+
+/* BlockPool::alloc / free / reset / num_blocks / num_free
+ * (page_attention.cpp:25-64) on the layer's K (which = 0) or V (which = 1)
+ * pool. alloc: most recently freed id first (LIFO), else the next never-used
+ * id; GKV_ERR_NO_PAGES at capacity (the reference returns -1, which *id also
+ * receives). free: ids never handed out are ignored, like the reference;
+ * freeing an id twice is rejected (GKV_ERR_INVALID), which the reference does
+ * not check. */
+int gkv_page_alloc(gkv_manager* m, int32_t layer_id, int32_t which, int32_t* id);
+int gkv_page_free(gkv_manager* m, int32_t layer_id, int32_t which, int32_t id);
+int gkv_pool_reset(gkv_manager* m, int32_t layer_id, int32_t which);
+int gkv_pool_stats(const gkv_manager* m, int32_t layer_id, int32_t which, int32_t* num_blocks,
+                   int32_t* num_free, int32_t* capacity);
+
+/* Read and clear the device error word of a layer (synchronises the layer's
+ * last stream): bit 0 = a page id outside the pool was skipped, bit 1 = a
+ * wait on an asynchronous copy timed out. *flags = 0 when clean. */
+int gkv_check_device_errors(gkv_manager* m, int32_t layer_id, uint32_t* flags);
+
+/* ======================= raw tier ======================================== */
+
+/* Device-resident block table of one layer plus its kernel scratch (split-K
+ * partials, per-head completion counters, error word). */
+typedef struct gkv_table gkv_table;
+
+int gkv_table_create(int device, int32_t capacity, gkv_table** out);
+int gkv_table_destroy(gkv_table* t);
+const int32_t* gkv_table_device_ptr(const gkv_table* t);
+/* Synchronise the table's device, read and clear its device error word (the
+ * bits of gkv_check_device_errors). */
+int gkv_table_check_errors(gkv_table* t, uint32_t* flags);
+
+/* A KV pool pair in the reference's page layout, managed by the caller. */
+typedef struct gkv_pool_desc {
+    void* k_base;
+    void* v_base;
+    int32_t pool_pages; /* pages addressable from each base (bounds for ids) */
+    int32_t n_kv_heads;
+    int32_t head_dim;
+    int32_t dtype;
+} gkv_pool_desc;
+
+/* The table delta of one step: logical pages [first_new_page, first_new_page +
+ * n_new_pages) were just allocated by the caller with these ids. The kernels
+ * write them into the device table; older entries must already be there. */
+typedef struct gkv_new_pages {
+    int32_t first_new_page;
+    int32_t n_new_pages;
+    const int32_t* k_ids; /* host arrays, n_new_pages entries */
+    const int32_t* v_ids;
+} gkv_new_pages;
+
+/* Scatter seq_len tokens of K/V (device [Hkv][seq_len][D]) into positions
+ * [n_prior, n_prior + seq_len) of the table. */
+int gkv_append_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior,
+                      const gkv_new_pages* np, const void* K, const void* V, int32_t seq_len,
+                      gkv_stream_t stream);
+
+/* Append, then attend; n_prior tokens were cached before the call. */
+int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior,
+                            const gkv_new_pages* np, const void* Q, const void* K, const void* V,
+                            void* out, int32_t n_q_heads, int32_t seq_len, float scale,
+                            int32_t causal, int32_t out_dtype, gkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,19 @@
+"""The golden cases: (name, fragmented_case kwargs, causal). Shared by the
+fixture generator (make_golden.py) and the tests that read the fixtures."""
+
+# Small cases store every input in the fixture; "config1" (Qwen3-0.6B layer,
+# seed 0, 1024 prior tokens in 64 of 256 pages, append 1) stores only the
+# outputs and checksums, its inputs being regenerated from the seed.
+SMALL = [
+    ("decode_g2_midpage", dict(seed=11, n_q_heads=4, n_kv_heads=2, head_dim=128, n_prior=37, pool_pages=8), True),
+    ("decode_g2_newpage", dict(seed=12, n_q_heads=4, n_kv_heads=2, head_dim=128, n_prior=48, pool_pages=8), True),
+    ("decode_g1", dict(seed=13, n_q_heads=2, n_kv_heads=2, head_dim=128, n_prior=21, pool_pages=6), True),
+    ("decode_g4", dict(seed=14, n_q_heads=8, n_kv_heads=2, head_dim=128, n_prior=70, pool_pages=8), True),
+    ("decode_g8", dict(seed=15, n_q_heads=8, n_kv_heads=1, head_dim=128, n_prior=33, pool_pages=6), True),
+    ("decode_first_token", dict(seed=16, n_q_heads=4, n_kv_heads=2, head_dim=128, n_prior=0, pool_pages=4), True),
+    ("chunk_causal", dict(seed=17, n_q_heads=4, n_kv_heads=2, head_dim=128, n_prior=10, pool_pages=8, n_new=29), True),
+    ("chunk_noncausal", dict(seed=18, n_q_heads=4, n_kv_heads=2, head_dim=128, n_prior=10, pool_pages=8, n_new=29), False),
+    ("chunk_from_empty", dict(seed=19, n_q_heads=4, n_kv_heads=2, head_dim=128, n_prior=0, pool_pages=8, n_new=40), True),
+]
+
+CONFIG1 = ("config1", dict(seed=0, n_q_heads=16, n_kv_heads=8, head_dim=128, n_prior=1024, pool_pages=256), True)
