@@ -1,45 +1,51 @@
 // decode.cu — fused paged-attention decode step for sm_100a.
 //
-// One launch does what the reference spreads over 2*Hkv synchronous
+// One step does what the reference spreads over 2*Hkv synchronous
 // cudaMemcpy calls, a cudaMalloc/H2D/cudaFree of the page ids and a
 // warp-per-head kernel with a serial page loop (src/core/page_attention.cpp:
-// 104-139, src/backend/cuda/attention.cu:401-580):
+// 104-139, src/backend/cuda/attention.cu:401-580). Two launches:
 //
-//   * grid (n_splits, Hkv): a CTA owns ONE kv head and a contiguous range of
-//     logical pages, and all G = Hq/Hkv query heads of that kv head, so every
-//     KV byte is read from HBM exactly once (GQA grouping);
-//   * each of its 4 warps runs its own TMA pipeline: R stages of one
-//     (page, head) K tile and V tile (16 slots x 128 x bf16 = 4 KiB each),
-//     loaded with cp.async.bulk.tensor (3-D map over the pool, box
-//     {128, 1, 16}, evict-first L2 policy) and completed on an mbarrier;
-//   * QK^T: a lane owns 4 of the 128 dims; per chunk of CH slots the CH*G
-//     partial dot products are reduced across the warp with a butterfly
-//     reduce-scatter (CH*G - 1 shuffles instead of 5 per score);
-//   * fp32 online softmax (log2 domain) and PV with the probabilities
-//     broadcast through shared memory;
+// paged_decode_kernel — one CTA per SM, each owning a contiguous range of
+// logical pages (split-K over the context):
+//   * a producer warp stages pages by TMA (no multicast): per page, per
+//     kv head, per 64-dim half one box {64 dims, 1 head, 16 slots} of the
+//     pool's 3-D map, 128-byte swizzle; a stage holds 8 (page, head) tiles of
+//     K and of V (64 KiB), three stages in flight; full/empty mbarriers;
+//   * 8 consumer warps, warp w on head (w % Hkv) of page (w / Hkv) of each
+//     stage, so all heads of a page are fetched together (whole page
+//     regions, DRAM-friendly) and every KV byte is read from HBM once;
+//   * per (page, head): S^T = K Q^T with mma.sync m16n8k16 (bf16 in, fp32
+//     accumulate; M = 16 slots, N = the G grouped query heads padded to 8,
+//     K = 128 dims in 8 steps, operands by ldmatrix from the swizzled tile),
+//     fp32 online softmax per head with 3-step warp shuffles (log2 domain),
+//     then O^T += V^T P^T (M = 16 dims x 8 tiles, K = 16 slots, ldmatrix.trans);
 //   * the step's new token (position n_prior) is taken from the K/V inputs,
-//     patched into the staged tile and written to its page in the pool by
-//     the warp that owns that page (the fused append);
-//   * warps merge in shared memory, CTAs write (m, l, acc) partials, and the
-//     last CTA of each kv head (atomic ticket) merges the splits and stores
-//     the output.
+//     patched into the staged tile and written to its page in the pool by the
+//     warp that owns that (page, head): the fused append;
+//   * warps merge in shared memory; each CTA writes an (m, l, acc) partial per
+//     query head.
+// paged_decode_combine_kernel — launched with programmatic dependent launch,
+// one CTA per query head merges the splits and stores the output.
 //
-// Page-id bounds are checked: a bad id is skipped and flags kErrBadPage.
-// Every mbarrier wait is bounded (kErrTimeout).
+// Page ids are bounds-checked (a bad id is skipped and sets kErrBadPage);
+// every mbarrier wait is bounded (kErrTimeout).
 #include "device.cuh"
 #include "kernels.h"
 
 namespace gkv {
 namespace {
 
-constexpr int kWarps = 4;       // consumer warps per CTA, each an independent pipeline
-constexpr int kStages = 3;      // TMA stages per warp
-constexpr int kTileBytes = kPageSlots * kHeadDim * 2;  // one (page, head) tile: 4 KiB
-constexpr int kStageBytes = 2 * kTileBytes;            // K + V
-constexpr int kTileRegion = kWarps * kStages * kStageBytes;
-constexpr int kSmemBytes = kTileRegion + kWarps * kStages * 8 + kWarps * 32 * 4;
-static_assert(kWarps * 32 == kHeadDim, "the merge maps one thread to one head dim");
-static_assert(kWarps * 8 * (kHeadDim + 2) * 4 <= kTileRegion, "merge buffers reuse the tiles");
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + producer warp
+constexpr int kStages = 3;
+constexpr uint32_t kTileHalf = kPageSlots * 128;     // 16 slots x 128 B (64 dims): 2 KiB
+constexpr uint32_t kTile = 2 * kTileHalf;            // one (page, head) K or V tile: 4 KiB
+constexpr uint32_t kStageKV = kConsumerWarps * kTile;  // 32 KiB of K (or V) per stage
+constexpr uint32_t kStageBytes = 2 * kStageKV;        // 64 KiB
+constexpr uint32_t kOffBar = kStages * kStageBytes;
+constexpr uint32_t kOffP = kOffBar + 2 * kStages * 8;            // per-warp P buffers
+constexpr uint32_t kSmemBytes = kOffP + kConsumerWarps * 256 + 1024;  // + alignment slack
+static_assert(kConsumerWarps * 8 * (kHeadDim + 2) * 4 <= kStages * kStageBytes, "merge buffers fit");
 
 struct DecodeParams {
     const uint16_t* q;
@@ -48,19 +54,17 @@ struct DecodeParams {
     uint16_t* k_base;
     uint16_t* v_base;
     int2* table;
-    void* out;
-    float* part_acc;
-    float2* part_ml;
-    uint32_t* counters;
+    float* part_acc;   // [n_splits][Hq][128]
+    float2* part_ml;   // [n_splits][Hq]
     uint32_t* err;
-    int32_t out_dtype;
     int32_t n_kv_heads;
+    int32_t group;     // G = Hq / Hkv
     int32_t pool_pages;
     int32_t n_prior;
     int32_t total;
     int32_t n_pages;
-    int32_t n_splits;
     int32_t pages_per_split;
+    int32_t pages_per_stage;  // P = 8 / Hkv (floored)
     int32_t new_first;
     int32_t new_n;
     float qscale;  // softmax scale * log2(e)
@@ -77,318 +81,345 @@ __device__ __forceinline__ bool entry_ok(const DecodeParams& a, int2 e) {
     return e.x >= 0 && e.x < a.pool_pages && e.y >= 0 && e.y < a.pool_pages;
 }
 
-// Butterfly reduce-scatter of NV per-lane partials (NV = 16 or 32): afterwards
-// lane l holds the full warp sum of value index (l >> (5 - log2 NV)).
-template <int NV>
-__device__ __forceinline__ float reduce_scatter(float (&v)[NV], int lane) {
-    int n = NV;
-#pragma unroll
-    for (int mask = 16; mask >= 1; mask >>= 1) {
-        if (n > 1) {
-            const bool upper = (lane & mask) != 0;
-#pragma unroll
-            for (int i = 0; i < NV / 2; ++i) {
-                if (i < n / 2) {
-                    const float send = upper ? v[i] : v[i + n / 2];
-                    const float keep = upper ? v[i + n / 2] : v[i];
-                    v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, mask);
-                }
-            }
-            n >>= 1;
-        } else {
-            v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], mask);
-        }
-    }
-    return v[0];
+// Byte offset of (slot row r, 16-byte chunk c of the 128 dims) inside a
+// (page, head) tile stored as two 128-byte-swizzled 64-dim halves.
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {
+    return (uint32_t)((c >> 3) * kTileHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-template <int G>
-__global__ void __launch_bounds__(kWarps * 32, 2)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap k_map,
-                        const __grid_constant__ CUtensorMap v_map, const DecodeParams a) {
-    constexpr int CH = (32 / G) < kPageSlots ? (32 / G) : kPageSlots;  // slots per chunk
-    constexpr int NV = CH * G;                                         // 16 or 32
-    constexpr int LOG_NV = NV == 32 ? 5 : 4;
-    constexpr int SH = 5 - LOG_NV;          // lane l holds value index l >> SH
-    constexpr int LOG_G = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
-    constexpr int SMASK0 = 1 << (SH + LOG_G);  // first lane mask spanning the slot bits
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
 
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileRegion);
-    float* pbuf_all = reinterpret_cast<float*>(bars + kWarps * kStages);
-    __shared__ uint32_t s_ticket;
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
+                        const DecodeParams a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* empty = full + kStages;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
     const int split = blockIdx.x;
     const int Hkv = a.n_kv_heads;
-
-    uint8_t* my_tiles = smem + warp * kStages * kStageBytes;
-    uint64_t* my_bars = bars + warp * kStages;
-    float* pbuf = pbuf_all + warp * 32;
-
+    const int G = a.group;
+    const int P = a.pages_per_stage;
     const int p0 = split * a.pages_per_split;
     const int p1 = min(a.n_pages, p0 + a.pages_per_split);
-    const int first = p0 + warp;
-    const int cnt = first < p1 ? (p1 - first + kWarps - 1) / kWarps : 0;
+    const int n_stages = p1 > p0 ? (p1 - p0 + P - 1) / P : 0;
 
-    if (lane == 0) {
-#pragma unroll
-        for (int s = 0; s < kStages; ++s) mbar_init(&my_bars[s], 1);
+    // Publish this step's new block-table entries (this launch reads them
+    // from its parameters; later launches read the table).
+    if (split == 0 && (int)threadIdx.x < a.new_n) a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
         fence_mbar_init();
     }
-    __syncwarp();
+    __syncthreads();
 
-    const uint64_t policy = l2_policy_evict_first();
-    auto issue = [&](int k) {  // lane 0: stage page `k` of this warp
-        const int lp = first + k * kWarps;
-        const int2 e = page_entry(a, lp);
-        uint64_t* bar = &my_bars[k % kStages];
-        uint8_t* dst = my_tiles + (k % kStages) * kStageBytes;
-        fence_proxy_async_smem();
-        if (entry_ok(a, e)) {
-            mbar_arrive_expect_tx(bar, kStageBytes);
-            tma_load_3d(dst, &k_map, bar, 0, h, e.x * kPageSlots, policy);
-            tma_load_3d(dst + kTileBytes, &v_map, bar, 0, h, e.y * kPageSlots, policy);
-        } else {
-            atomicOr(a.err, kErrBadPage);
-            mbar_arrive(bar);
-        }
-    };
-
-    if (lane == 0) {
-        const int pre = cnt < kStages ? cnt : kStages;
-        for (int k = 0; k < pre; ++k) issue(k);
-    }
-
-    // This lane's 4 dims of each grouped query head, pre-scaled to log2 units.
-    float qf[G][4];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const uint2 raw =
-            *reinterpret_cast<const uint2*>(a.q + (size_t)(h * G + g) * kHeadDim + lane * 4);
-        qf[g][0] = bf16_lo(raw.x) * a.qscale;
-        qf[g][1] = bf16_hi(raw.x) * a.qscale;
-        qf[g][2] = bf16_lo(raw.y) * a.qscale;
-        qf[g][3] = bf16_hi(raw.y) * a.qscale;
-    }
-
-    float m[G], l[G], acc[G][4];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-        acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-    }
-
-    const int my_v = lane >> SH;
-    const int my_s = my_v / G;
-    const int my_g = my_v % G;
-    bool timed_out = false;
-    int consumed = 0;
-
-    for (int k = 0; k < cnt; ++k) {
-        const int st = k % kStages;
-        const uint32_t parity = (k / kStages) & 1;
-        const int lp = first + k * kWarps;
-        const int2 e = page_entry(a, lp);
-        const bool ok = entry_ok(a, e);
-        if (!mbar_wait_bounded(&my_bars[st], parity)) {
-            timed_out = true;
-            break;
-        }
-        consumed = k + 1;
-        uint16_t* kt = reinterpret_cast<uint16_t*>(my_tiles + st * kStageBytes);
-        uint16_t* vt = kt + kPageSlots * kHeadDim;
-        const int base = lp * kPageSlots;
-        const int nvalid = min(kPageSlots, a.total - base);
-
-        // Fused append: the step's token lands in this page.
-        if (a.k_new != nullptr && a.n_prior >= base && a.n_prior < base + kPageSlots) {
-            const int slot = a.n_prior - base;
-            const uint2 kk = *reinterpret_cast<const uint2*>(a.k_new + (size_t)h * kHeadDim + lane * 4);
-            const uint2 vv = *reinterpret_cast<const uint2*>(a.v_new + (size_t)h * kHeadDim + lane * 4);
-            *reinterpret_cast<uint2*>(kt + slot * kHeadDim + lane * 4) = kk;
-            *reinterpret_cast<uint2*>(vt + slot * kHeadDim + lane * 4) = vv;
-            if (ok) {
-                const size_t row = ((size_t)slot * Hkv + h) * kHeadDim + lane * 4;
-                *reinterpret_cast<uint2*>(a.k_base + (size_t)e.x * kPageSlots * Hkv * kHeadDim + row) = kk;
-                *reinterpret_cast<uint2*>(a.v_base + (size_t)e.y * kPageSlots * Hkv * kHeadDim + row) = vv;
-            }
-            __syncwarp();
-        }
-
-        if (ok) {
-#pragma unroll
-            for (int c = 0; c < kPageSlots / CH; ++c) {
-                const int s0 = c * CH;
-                if (s0 >= nvalid) break;
-                float part[NV];
-#pragma unroll
-                for (int s = 0; s < CH; ++s) {
-                    const uint2 raw = *reinterpret_cast<const uint2*>(kt + (s0 + s) * kHeadDim + lane * 4);
-                    const float k0 = bf16_lo(raw.x), k1 = bf16_hi(raw.x);
-                    const float k2 = bf16_lo(raw.y), k3 = bf16_hi(raw.y);
-#pragma unroll
-                    for (int g = 0; g < G; ++g)
-                        part[s * G + g] = fmaf(qf[g][3], k3, fmaf(qf[g][2], k2, fmaf(qf[g][1], k1, qf[g][0] * k0)));
+    if (warp == kConsumerWarps) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            for (int i = 0; i < n_stages; ++i) {
+                const int st = i % kStages;
+                if (i >= kStages && !mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1)) {
+                    atomicOr(a.err, kErrTimeout);
                 }
-                float sc = reduce_scatter<NV>(part, lane);
-                if (s0 + my_s >= nvalid) sc = -INFINITY;
-
-                float cmax = sc;
-#pragma unroll
-                for (int mask = SMASK0; mask <= 16; mask <<= 1)
-                    cmax = fmaxf(cmax, __shfl_xor_sync(0xFFFFFFFFu, cmax, mask));
-                float mnew[G];
-                float m_own = 0.f;
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    mnew[g] = fmaxf(m[g], __shfl_sync(0xFFFFFFFFu, cmax, g << SH));
-                    if (g == my_g) m_own = mnew[g];
-                }
-                const float p = (sc == -INFINITY) ? 0.f : exp2_approx(sc - m_own);
-                float psum = p;
-#pragma unroll
-                for (int mask = SMASK0; mask <= 16; mask <<= 1)
-                    psum += __shfl_xor_sync(0xFFFFFFFFu, psum, mask);
-                if ((lane & ((1 << SH) - 1)) == 0) pbuf[my_v] = p;
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float alpha = (mnew[g] == -INFINITY) ? 1.f : exp2_approx(m[g] - mnew[g]);
-                    l[g] = l[g] * alpha + __shfl_sync(0xFFFFFFFFu, psum, g << SH);
-                    acc[g][0] *= alpha;
-                    acc[g][1] *= alpha;
-                    acc[g][2] *= alpha;
-                    acc[g][3] *= alpha;
-                    m[g] = mnew[g];
-                }
-                __syncwarp();
-#pragma unroll
-                for (int s = 0; s < CH; ++s) {
-                    if (s0 + s < nvalid) {
-                        const uint2 raw = *reinterpret_cast<const uint2*>(vt + (s0 + s) * kHeadDim + lane * 4);
-                        const float v0 = bf16_lo(raw.x), v1 = bf16_hi(raw.x);
-                        const float v2 = bf16_lo(raw.y), v3 = bf16_hi(raw.y);
-#pragma unroll
-                        for (int g = 0; g < G; ++g) {
-                            const float pg = pbuf[s * G + g];
-                            acc[g][0] = fmaf(pg, v0, acc[g][0]);
-                            acc[g][1] = fmaf(pg, v1, acc[g][1]);
-                            acc[g][2] = fmaf(pg, v2, acc[g][2]);
-                            acc[g][3] = fmaf(pg, v3, acc[g][3]);
+                uint8_t* sk = smem + st * kStageBytes;
+                uint8_t* sv = sk + kStageKV;
+                const int np = min(P, p1 - (p0 + i * P));
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(&full[st], (uint32_t)(np * Hkv) * 2u * kTile);
+                for (int pi = 0; pi < np; ++pi) {
+                    int2 e = page_entry(a, p0 + i * P + pi);
+                    if (!entry_ok(a, e)) {
+                        atomicOr(a.err, kErrBadPage);
+                        e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
+                    }
+                    for (int h = 0; h < Hkv; ++h) {
+                        const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
+                        for (int hf = 0; hf < 2; ++hf) {
+                            tma_load_3d(sk + t + hf * kTileHalf, &k_map, &full[st], hf * 64, h, e.x * kPageSlots, pol);
+                            tma_load_3d(sv + t + hf * kTileHalf, &v_map, &full[st], hf * 64, h, e.y * kPageSlots, pol);
                         }
                     }
                 }
-                __syncwarp();
             }
         }
+    } else {
+        // ---------------- consumers ----------------
+        const int head = warp % Hkv;
+        const int pslot = warp / Hkv;           // page within a stage
+        const bool active = pslot < P;
+        const int g = lane >> 2;                // fragment row group
+        const int t = lane & 3;                 // fragment column pair
+        uint8_t* pbuf = smem + kOffP + warp * 256;  // P^T staging: [8 heads][16 slots] bf16
+
+        // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
+        uint32_t qb[8][2];
+        {
+            const int n = g;
+            const bool valid = active && n < G;
+            const uint16_t* qr = a.q + (size_t)(head * G + (valid ? n : 0)) * kHeadDim;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                qb[kk][0] = valid ? *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 2 * t) : 0u;
+                qb[kk][1] = valid ? *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 2 * t + 8) : 0u;
+            }
+        }
+        float acc[8][4];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2t, 2t+1
+
+        // ldmatrix row addressing (lane -> matrix mi, row within it).
+        const int mi = lane >> 3;
+        const int lr = lane & 7;
+
+        for (int i = 0; i < n_stages; ++i) {
+            const int st = i % kStages;
+            const bool ok_wait = mbar_wait_bounded(&full[st], (i / kStages) & 1);
+            if (!ok_wait && lane == 0) atomicOr(a.err, kErrTimeout);
+            const int lp = p0 + i * P + pslot;
+            const bool have = active && lp < p1 && ok_wait;
+            int2 e = have ? page_entry(a, lp) : make_int2(0, 0);
+            const bool use = have && entry_ok(a, e);
+            if (use) {
+                uint8_t* kt = smem + st * kStageBytes + (uint32_t)(pslot * Hkv + head) * kTile;
+                uint8_t* vt = kt + kStageKV;
+                const int base = lp * kPageSlots;
+                const int nvalid = min(kPageSlots, a.total - base);
+                // Fused append of this step's token.
+                if (a.k_new != nullptr && a.n_prior >= base && a.n_prior < base + kPageSlots) {
+                    const int slot = a.n_prior - base;
+                    const uint2 kk = *reinterpret_cast<const uint2*>(a.k_new + (size_t)head * kHeadDim + lane * 4);
+                    const uint2 vv = *reinterpret_cast<const uint2*>(a.v_new + (size_t)head * kHeadDim + lane * 4);
+                    const uint32_t o = tile_off(slot, lane >> 1) + (lane & 1) * 8;
+                    *reinterpret_cast<uint2*>(kt + o) = kk;
+                    *reinterpret_cast<uint2*>(vt + o) = vv;
+                    const size_t row = ((size_t)slot * Hkv + head) * kHeadDim + lane * 4;
+                    *reinterpret_cast<uint2*>(a.k_base + (size_t)e.x * kPageSlots * Hkv * kHeadDim + row) = kk;
+                    *reinterpret_cast<uint2*>(a.v_base + (size_t)e.y * kPageSlots * Hkv * kHeadDim + row) = vv;
+                }
+                // Slots past the cache: zero their V rows (0 x NaN would poison the MMA).
+                if (nvalid < kPageSlots) {
+                    for (int r = nvalid + (lane >> 3); r < kPageSlots; r += 4) {
+                        *reinterpret_cast<uint4*>(vt + r * 128 + (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(vt + kTileHalf + r * 128 + (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                __syncwarp();
+
+                // S^T[slot][head] = K Q^T
+                float s[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint32_t ks = smem_addr(kt);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+                    mma_bf16_16816(s, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+                }
+                // s[0]: (slot g, head 2t) s[1]: (g, 2t+1) s[2]: (g+8, 2t) s[3]: (g+8, 2t+1)
+                const bool v_lo = g < nvalid, v_hi = g + 8 < nvalid;
+                const float s0 = v_lo ? s[0] * a.qscale : -INFINITY;
+                const float s1 = v_lo ? s[1] * a.qscale : -INFINITY;
+                const float s2 = v_hi ? s[2] * a.qscale : -INFINITY;
+                const float s3 = v_hi ? s[3] * a.qscale : -INFINITY;
+                float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+                for (int m = 4; m <= 16; m <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, m));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, m));
+                }
+                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);  // finite: slot 0 is always valid
+                const float al0 = exp2_approx(m0 - mn0), al1 = exp2_approx(m1 - mn1);
+                const float p0v = exp2_approx(s0 - mn0), p1v = exp2_approx(s1 - mn1);
+                const float p2v = exp2_approx(s2 - mn0), p3v = exp2_approx(s3 - mn1);
+                float su0 = p0v + p2v, su1 = p1v + p3v;
+#pragma unroll
+                for (int m = 4; m <= 16; m <<= 1) {
+                    su0 += __shfl_xor_sync(0xFFFFFFFFu, su0, m);
+                    su1 += __shfl_xor_sync(0xFFFFFFFFu, su1, m);
+                }
+                l0 = l0 * al0 + su0;
+                l1 = l1 * al1 + su1;
+                m0 = mn0;
+                m1 = mn1;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    acc[mt][0] *= al0;
+                    acc[mt][1] *= al1;
+                    acc[mt][2] *= al0;
+                    acc[mt][3] *= al1;
+                }
+                // P^T staging: pbuf[head][slot] (bf16), then B fragments of O^T += V^T P^T.
+                uint16_t* pb = reinterpret_cast<uint16_t*>(pbuf);
+                const uint32_t w01 = pack_bf16x2(p0v, p1v), w23 = pack_bf16x2(p2v, p3v);
+                pb[(2 * t) * 16 + g] = (uint16_t)(w01 & 0xFFFFu);
+                pb[(2 * t + 1) * 16 + g] = (uint16_t)(w01 >> 16);
+                pb[(2 * t) * 16 + g + 8] = (uint16_t)(w23 & 0xFFFFu);
+                pb[(2 * t + 1) * 16 + g + 8] = (uint16_t)(w23 >> 16);
+                __syncwarp();
+                const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(pb + g * 16 + 2 * t);
+                const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(pb + g * 16 + 2 * t + 8);
+                const uint32_t vs = smem_addr(vt);
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(vs + tile_off(lr + (mi >> 1) * 8, 2 * mt + (mi & 1)), a0, a1, a2, a3);
+                    mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+                }
+                fence_proxy_async_smem();  // generic writes above precede the next TMA into this stage
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+
+        // Per-warp state to shared memory (stage buffers are free: the producer
+        // issued nothing beyond n_stages and every stage was consumed).
         __syncwarp();
-        if (lane == 0 && k + kStages < cnt) issue(k + kStages);
-    }
-
-    if (timed_out) {
-        // Drain this warp's copies still in flight (bounded) before exiting.
-        if (lane == 0) atomicOr(a.err, kErrTimeout);
-        const int issued = cnt < consumed + kStages ? cnt : consumed + kStages;
-        for (int k = consumed; k < issued; ++k)
-            (void)mbar_wait_bounded(&my_bars[k % kStages], (k / kStages) & 1);
-    }
-
-    // ---- merge the warps of this CTA -----------------------------------
-    __syncthreads();
-    float* w_acc = reinterpret_cast<float*>(smem);  // [kWarps][G][128]
-    float* w_m = w_acc + kWarps * G * kHeadDim;     // [kWarps][G]
-    float* w_l = w_m + kWarps * G;
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+        float* w_acc = reinterpret_cast<float*>(smem);  // [warp][8 heads][128]
+        float* w_ml = w_acc + kConsumerWarps * 8 * kHeadDim;  // [warp][8 heads][2]
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        *reinterpret_cast<float4*>(&w_acc[(warp * G + g) * kHeadDim + lane * 4]) =
-            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-        if (lane == 0) {
-            w_m[warp * G + g] = m[g];
-            w_l[warp * G + g] = l[g];
+        for (int mt = 0; mt < 8; ++mt) {
+            const int d = mt * 16 + g;
+            w_acc[(warp * 8 + 2 * t) * kHeadDim + d] = acc[mt][0];
+            w_acc[(warp * 8 + 2 * t + 1) * kHeadDim + d] = acc[mt][1];
+            w_acc[(warp * 8 + 2 * t) * kHeadDim + d + 8] = acc[mt][2];
+            w_acc[(warp * 8 + 2 * t + 1) * kHeadDim + d + 8] = acc[mt][3];
+        }
+        if (g == 0) {
+            w_ml[(warp * 8 + 2 * t) * 2 + 0] = active ? m0 : -INFINITY;
+            w_ml[(warp * 8 + 2 * t) * 2 + 1] = active ? l0 : 0.f;
+            w_ml[(warp * 8 + 2 * t + 1) * 2 + 0] = active ? m1 : -INFINITY;
+            w_ml[(warp * 8 + 2 * t + 1) * 2 + 1] = active ? l1 : 0.f;
         }
     }
     __syncthreads();
 
-    const int d = threadIdx.x;  // kWarps * 32 == kHeadDim threads: one dim each
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, w_m[w * G + g]);
-        const float Ms = (M == -INFINITY) ? 0.f : M;
-        float L = 0.f, A = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            const float f = exp2_approx(w_m[w * G + g] - Ms);
-            L = fmaf(w_l[w * G + g], f, L);
-            A = fmaf(w_acc[(w * G + g) * kHeadDim + d], f, A);
-        }
-        const int hq = h * G + g;
-        if (a.n_splits == 1) {
-            store_out(a.out, (size_t)hq * kHeadDim + d, A / L, a.out_dtype);
-        } else {
-            const size_t row = (size_t)hq * a.n_splits + split;
+    // ---- merge warps of the same head; write this split's partials ---------
+    {
+        float* w_acc = reinterpret_cast<float*>(smem);
+        float* w_ml = w_acc + kConsumerWarps * 8 * kHeadDim;
+        const int Hq = Hkv * G;
+        const int n_warps_used = min(kConsumerWarps, P * Hkv);
+        for (int idx = threadIdx.x; idx < Hq * kHeadDim; idx += kThreads) {
+            const int hq = idx / kHeadDim, d = idx % kHeadDim;
+            const int h = hq / G, gg = hq % G;
+            float M = -INFINITY;
+            for (int w = h; w < n_warps_used; w += Hkv) M = fmaxf(M, w_ml[(w * 8 + gg) * 2]);
+            const float Ms = M == -INFINITY ? 0.f : M;
+            float L = 0.f, A = 0.f;
+            for (int w = h; w < n_warps_used; w += Hkv) {
+                const float f = exp2_approx(w_ml[(w * 8 + gg) * 2] - Ms);
+                L = fmaf(w_ml[(w * 8 + gg) * 2 + 1], f, L);
+                A = fmaf(w_acc[(w * 8 + gg) * kHeadDim + d], f, A);
+            }
+            const size_t row = (size_t)split * Hq + hq;
             a.part_acc[row * kHeadDim + d] = A;
             if (d == 0) a.part_ml[row] = make_float2(M, L);
         }
     }
-    if (a.n_splits == 1) return;
-
-    // ---- last CTA of this kv head merges the splits -----------------------
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[h], 1u);
-    __syncthreads();
-    if (s_ticket != (uint32_t)(a.n_splits - 1)) return;
-    __threadfence();
-#pragma unroll 1
-    for (int g = 0; g < G; ++g) {
-        const int hq = h * G + g;
-        const float2* ml = a.part_ml + (size_t)hq * a.n_splits;
-        const float* pa = a.part_acc + (size_t)hq * a.n_splits * kHeadDim + d;
-        float M = -INFINITY;
-        for (int s = 0; s < a.n_splits; ++s) M = fmaxf(M, __ldcg(&ml[s].x));
-        const float Ms = (M == -INFINITY) ? 0.f : M;
-        float L = 0.f, A = 0.f;
-        for (int s = 0; s < a.n_splits; ++s) {
-            const float2 e = __ldcg(&ml[s]);
-            const float f = exp2_approx(e.x - Ms);
-            L = fmaf(e.y, f, L);
-            A = fmaf(__ldcg(&pa[(size_t)s * kHeadDim]), f, A);
-        }
-        store_out(a.out, (size_t)hq * kHeadDim + d, A / L, a.out_dtype);
-    }
-    if (threadIdx.x == 0) a.counters[h] = 0u;  // ready for the next launch
+    // Let the combine kernel (programmatic dependent launch) start its prologue.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <int G>
-cudaError_t launch_g(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p,
-                     dim3 grid, cudaStream_t stream) {
-    // The shared-memory opt-in is per device; remember which devices have it.
+struct CombineParams {
+    const float* part_acc;
+    const float2* part_ml;
+    void* out;
+    int32_t out_dtype;
+    int32_t n_q_heads;
+    int32_t n_splits;
+};
+
+// One CTA per query head, one thread per dim: merge the splits' (m, l, acc).
+__global__ void __launch_bounds__(kHeadDim) paged_decode_combine_kernel(const CombineParams c) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
+    const int hq = blockIdx.x, d = threadIdx.x;
+    __shared__ float s_f[1024];
+    __shared__ float s_m[kHeadDim / 32];
+    __shared__ float s_l[kHeadDim / 32];
+    __shared__ float s_inv;
+    float M = -INFINITY;
+    for (int s = threadIdx.x; s < c.n_splits; s += kHeadDim) M = fmaxf(M, c.part_ml[(size_t)s * c.n_q_heads + hq].x);
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, m));
+    if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = M;
+    __syncthreads();
+    M = s_m[0];
+    for (int w = 1; w < kHeadDim / 32; ++w) M = fmaxf(M, s_m[w]);
+    const float Ms = M == -INFINITY ? 0.f : M;
+    float L = 0.f;
+    for (int s = threadIdx.x; s < c.n_splits; s += kHeadDim) {
+        const float2 ml = c.part_ml[(size_t)s * c.n_q_heads + hq];
+        const float f = exp2_approx(ml.x - Ms);
+        if (s < 1024) s_f[s] = f;
+        L = fmaf(ml.y, f, L);
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, m);
+    if ((threadIdx.x & 31) == 0) s_l[threadIdx.x >> 5] = L;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < kHeadDim / 32; ++w) tot += s_l[w];
+        s_inv = 1.f / tot;
+    }
+    __syncthreads();
+    float A = 0.f;
+    for (int s = 0; s < c.n_splits; ++s) {
+        const float f = s < 1024 ? s_f[s] : exp2_approx(c.part_ml[(size_t)s * c.n_q_heads + hq].x - Ms);
+        A = fmaf(c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d], f, A);
+    }
+    store_out(c.out, (size_t)hq * kHeadDim + d, A * s_inv, c.out_dtype);
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map, int2* table,
+                          const NewPages& np, const Scratch& scratch, const DecodeLaunch& d, int num_sms,
+                          cudaStream_t stream) {
+    const int Hkv = pool.n_kv_heads;
+    if (Hkv > kConsumerWarps) return cudaErrorInvalidValue;
     static unsigned long long configured = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 64 || !(configured & (1ull << dev))) {
-        e = cudaFuncSetAttribute(paged_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kSmemBytes);
+        e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
-    paged_decode_kernel<G><<<grid, kWarps * 32, kSmemBytes, stream>>>(km, vm, p);
-    return cudaGetLastError();
-}
-
-}  // namespace
-
-cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map,
-                          int2* table, const NewPages& np, const Scratch& scratch,
-                          const DecodeLaunch& d, int num_sms, cudaStream_t stream) {
-    const int Hkv = pool.n_kv_heads;
-    const int G = d.n_q_heads / Hkv;
     DecodeParams p;
     p.q = d.q;
     p.k_new = d.k_new;
@@ -396,47 +427,48 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     p.k_base = pool.k_base;
     p.v_base = pool.v_base;
     p.table = table;
-    p.out = d.out;
     p.part_acc = scratch.part_acc;
     p.part_ml = scratch.part_ml;
-    p.counters = scratch.counters;
     p.err = scratch.err;
-    p.out_dtype = d.out_dtype;
     p.n_kv_heads = Hkv;
+    p.group = d.n_q_heads / Hkv;
     p.pool_pages = pool.pool_pages;
     p.n_prior = d.n_prior;
     p.total = d.total;
     p.n_pages = d.n_pages;
+    p.pages_per_stage = kConsumerWarps / Hkv;
     p.qscale = d.scale * 1.4426950408889634f;
     p.new_first = np.first;
     p.new_n = np.n;
     for (int i = 0; i < np.n; ++i) p.new_ids[i] = np.ids[i];
 
-    // Splits: two resident CTAs per SM over all kv heads, at least one page
-    // per warp, and within the partials capacity.
-    int n_splits = d.n_splits;
-    if (n_splits <= 0) {
-        n_splits = (2 * num_sms + Hkv - 1) / Hkv;
-        const int by_pages = (d.n_pages + kWarps - 1) / kWarps;
-        if (n_splits > by_pages) n_splits = by_pages;
-    }
+    // One CTA per SM; each split a whole number of stages.
+    const int P = p.pages_per_stage;
+    const int n_stages_total = (d.n_pages + P - 1) / P;
+    int n_splits = d.n_splits > 0 ? d.n_splits : num_sms;
+    if (n_splits > n_stages_total) n_splits = n_stages_total;
     if (n_splits * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / d.n_q_heads;
     if (n_splits < 1) n_splits = 1;
-    int pps = (d.n_pages + n_splits - 1) / n_splits;
-    if (pps < 1) pps = 1;
-    n_splits = (d.n_pages + pps - 1) / pps;  // no empty splits
-    if (n_splits < 1) n_splits = 1;
-    p.n_splits = n_splits;
-    p.pages_per_split = pps;
+    const int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
+    p.pages_per_split = stages_per_split * P;
+    n_splits = (d.n_pages + p.pages_per_split - 1) / p.pages_per_split;
 
-    dim3 grid(n_splits, Hkv);
-    switch (G) {
-        case 1: return launch_g<1>(k_map, v_map, p, grid, stream);
-        case 2: return launch_g<2>(k_map, v_map, p, grid, stream);
-        case 4: return launch_g<4>(k_map, v_map, p, grid, stream);
-        case 8: return launch_g<8>(k_map, v_map, p, grid, stream);
-        default: return cudaErrorInvalidValue;
-    }
+    paged_decode_kernel<<<n_splits, kThreads, kSmemBytes, stream>>>(k_map, v_map, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(d.n_q_heads);
+    cfg.blockDim = dim3(kHeadDim);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel, c);
 }
 
 }  // namespace gkv

@@ -2,6 +2,7 @@
 // policies, bounded waits and the number-format conversions the path needs.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

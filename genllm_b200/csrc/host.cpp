@@ -20,6 +20,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -81,6 +82,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+// GKV_PREFILL_KERNEL=simt selects the CUDA-core prefill kernel instead of the
+// tensor-core one (a cross-check of two independent implementations).
+bool prefill_on_cuda_cores() {
+    static const bool simt = [] {
+        const char* v = getenv("GKV_PREFILL_KERNEL");
+        return v && std::strcmp(v, "simt") == 0;
+    }();
+    return simt;
+}
+
 bool is_out_dtype(int d) { return d == GKV_F32 || d == GKV_F16 || d == GKV_BF16; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -89,31 +100,38 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 namespace gkv {
 
-bool encode_pool_maps(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
+static bool encode(CUtensorMap* m, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, CUtensorMapSwizzle swz, const char** why) {
     auto enc = tensor_map_encoder();
     if (!enc) {
         *why = "cuTensorMapEncodeTiled unavailable";
         return false;
     }
-    // dims (fastest first): head dim, kv head, slot row over the whole pool.
-    cuuint64_t dims[3] = {(cuuint64_t)gkv::kHeadDim, (cuuint64_t)pool.n_kv_heads,
-                          (cuuint64_t)pool.pool_pages * 16};
-    cuuint64_t strides[2] = {(cuuint64_t)gkv::kHeadDim * 2,
-                             (cuuint64_t)pool.n_kv_heads * gkv::kHeadDim * 2};
-    cuuint32_t box[3] = {(cuuint32_t)gkv::kHeadDim, 1, 16};
-    cuuint32_t estr[3] = {1, 1, 1};
-    for (int i = 0; i < 2; ++i) {
-        CUtensorMap* m = i == 0 ? k_map : v_map;
-        void* base = i == 0 ? pool.k_base : pool.v_base;
-        CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) {
-            *why = "cuTensorMapEncodeTiled failed";
-            return false;
-        }
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *why = "cuTensorMapEncodeTiled failed";
+        return false;
     }
     return true;
+}
+
+bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)pool.n_kv_heads, (cuuint64_t)pool.pool_pages * 16};
+    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)pool.n_kv_heads * kHeadDim * 2};
+    cuuint32_t box[3] = {64, 1, 16};
+    return encode(k_map, pool.k_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why) &&
+           encode(v_map, pool.v_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
+}
+
+bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, CUtensorMap* q_map,
+                        const char** why) {
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)seq_len, (cuuint64_t)n_q_heads};
+    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)seq_len * kHeadDim * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    return encode(q_map, const_cast<uint16_t*>(q), 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
 }
 
 }  // namespace gkv
@@ -131,8 +149,8 @@ struct gkv_table {
     void* map_v_base = nullptr;
     int32_t map_pages = -1;
     int32_t map_heads = -1;
-    CUtensorMap k_map;
-    CUtensorMap v_map;
+    CUtensorMap k_map_sw;   // box {64 dims, 1 head, 16 slots}, 128-byte swizzle
+    CUtensorMap v_map_sw;
 };
 
 namespace {
@@ -141,7 +159,6 @@ void table_free(gkv_table* t) {
     cudaFree(t->d_table);
     cudaFree(t->scratch.part_acc);
     cudaFree(t->scratch.part_ml);
-    cudaFree(t->scratch.counters);
     cudaFree(t->scratch.err);
 }
 
@@ -168,7 +185,8 @@ int table_maps(gkv_table* t, const gkv_pool_desc* pool) {
     gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
                      pool->pool_pages, pool->n_kv_heads};
     const char* why = nullptr;
-    if (!gkv::encode_pool_maps(pv, &t->k_map, &t->v_map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
+    if (!gkv::encode_pool_maps_sw128(pv, &t->k_map_sw, &t->v_map_sw, &why))
+        return fail(GKV_ERR_CUDA, "%s", why);
     t->map_k_base = pool->k_base;
     t->map_v_base = pool->v_base;
     t->map_pages = pool->pool_pages;
@@ -279,15 +297,12 @@ int gkv_table_create(int device, int32_t capacity, gkv_table** out) {
         (e = cudaMemset(t->d_table, 0xFF, sizeof(int2) * (size_t)capacity)) != cudaSuccess ||
         (e = cudaMalloc(&t->scratch.part_acc, sizeof(float) * gkv::kMaxPartialRows * 128)) != cudaSuccess ||
         (e = cudaMalloc(&t->scratch.part_ml, sizeof(float2) * gkv::kMaxPartialRows)) != cudaSuccess ||
-        (e = cudaMalloc(&t->scratch.counters, sizeof(uint32_t) * kMaxKvHeads)) != cudaSuccess ||
-        (e = cudaMemset(t->scratch.counters, 0, sizeof(uint32_t) * kMaxKvHeads)) != cudaSuccess ||
         (e = cudaMalloc(&t->scratch.err, sizeof(uint32_t))) != cudaSuccess ||
         (e = cudaMemset(t->scratch.err, 0, sizeof(uint32_t))) != cudaSuccess) {
         table_free(t);
         delete t;
         return cuda_fail(e, "gkv_table_create");
     }
-    t->scratch.counters_len = kMaxKvHeads;
     *out = t;
     return GKV_OK;
 }
@@ -359,6 +374,9 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
                      pool->pool_pages, pool->n_kv_heads};
 
     if (seq_len == 1) {
+        if (pool->n_kv_heads > 8)
+            return fail(GKV_ERR_UNSUPPORTED, "decode kernel built for at most 8 kv heads per GPU (got %d)",
+                        pool->n_kv_heads);
         // Entries beyond the last 64 go first through table-only launches.
         const int32_t n_new = np ? np->n_new_pages : 0;
         const int32_t keep = std::min<int32_t>(n_new, gkv::kMaxNewPagesPerLaunch);
@@ -376,7 +394,7 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
         d.n_pages = n_pages;
         d.scale = scale;
         d.n_splits = 0;
-        cudaError_t e = gkv::launch_decode(pv, t->k_map, t->v_map, t->d_table, p, t->scratch, d, t->num_sms, s);
+        cudaError_t e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s);
         if (e != cudaSuccess) return cuda_fail(e, "decode launch");
         return GKV_OK;
     }
@@ -392,7 +410,15 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
     pl.n_pages = n_pages;
     pl.scale = scale;
     pl.causal = causal ? 1 : 0;
-    cudaError_t e = gkv::launch_prefill(pv, t->k_map, t->v_map, t->d_table, pl, t->scratch.err, t->num_sms, s);
+    cudaError_t e;
+    if (prefill_on_cuda_cores()) {
+        e = gkv::launch_prefill_simt(pv, t->d_table, pl, t->scratch.err, s);
+    } else {
+        CUtensorMap q_map;
+        const char* why = nullptr;
+        if (!gkv::encode_q_map_sw128(pl.q, n_q_heads, seq_len, &q_map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
+        e = gkv::launch_prefill_tc(pv, q_map, t->k_map_sw, t->v_map_sw, t->d_table, pl, t->scratch.err, s);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
     return GKV_OK;
 }

@@ -21,14 +21,12 @@ struct NewPages {
 };
 
 // Split-K partials capacity (q-head rows x splits) of one scratch area.
-constexpr int kMaxPartialRows = 4096;
+constexpr int kMaxPartialRows = 10240;
 
 struct Scratch {
-    float* part_acc;     // [kMaxPartialRows][128] un-normalised outputs
+    float* part_acc;     // [kMaxPartialRows][128] un-normalised split outputs
     float2* part_ml;     // [kMaxPartialRows] (running max in log2 units, sum)
-    uint32_t* counters;  // [n_kv_heads] split completion tickets, zero between launches
     uint32_t* err;       // device error word
-    int32_t counters_len;
 };
 
 struct PoolView {
@@ -38,9 +36,6 @@ struct PoolView {
     int32_t n_kv_heads;
 };
 
-// Encode the 3-D tensor maps (D, Hkv, pool_pages*16) over a K or V pool.
-bool encode_pool_maps(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map,
-                      const char** why);
 
 struct DecodeLaunch {
     const uint16_t* q;      // [Hq][128]
@@ -57,7 +52,8 @@ struct DecodeLaunch {
 };
 
 // Fused decode step: append one token's K/V, GQA-grouped split-K
-// flash-decoding over the block table, split combine. Returns the CUDA error.
+// flash-decoding over the block table (k_map/v_map: the pool's 128-byte
+// swizzled maps), then the split combine. Returns the CUDA error.
 cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map,
                           int2* table, const NewPages& np, const Scratch& scratch,
                           const DecodeLaunch& d, int num_sms, cudaStream_t stream);
@@ -82,10 +78,23 @@ struct PrefillLaunch {
     int32_t causal;
 };
 
+// Tensor maps of the tensor-core prefill: the pool's K/V with 128-byte
+// swizzle, box {64, 1, 16}; the chunk's Q [Hq][S][128], box {64, 128, 1}.
+bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map,
+                            const char** why);
+bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, CUtensorMap* q_map,
+                        const char** why);
+
 // Attention of a chunk of seq_len queries over the cached pages (the chunk's
-// own K/V already appended).
-cudaError_t launch_prefill(const PoolView& pool, const CUtensorMap& k_map,
-                           const CUtensorMap& v_map, const int2* table, const PrefillLaunch& p,
-                           uint32_t* err, int num_sms, cudaStream_t stream);
+// own K/V already appended), on the tensor cores.
+cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map,
+                              const CUtensorMap& k_map, const CUtensorMap& v_map,
+                              const int2* table, const PrefillLaunch& p, uint32_t* err,
+                              cudaStream_t stream);
+
+// The same on CUDA cores (one warp per query row); kept as an independent
+// second implementation for cross-checking.
+cudaError_t launch_prefill_simt(const PoolView& pool, const int2* table, const PrefillLaunch& p,
+                                uint32_t* err, cudaStream_t stream);
 
 }  // namespace gkv

@@ -107,13 +107,4 @@ cudaError_t launch_prefill_simt(const PoolView& pool, const int2* table, const P
     return cudaGetLastError();
 }
 
-cudaError_t launch_prefill(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map,
-                           const int2* table, const PrefillLaunch& p, uint32_t* err, int num_sms,
-                           cudaStream_t stream) {
-    (void)k_map;
-    (void)v_map;
-    (void)num_sms;
-    return launch_prefill_simt(pool, table, p, err, stream);
-}
-
 }  // namespace gkv

@@ -1,0 +1,329 @@
+// prefill_tc.cu — chunked-prefill paged attention on the 5th-generation
+// tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// The reference has no tensor-core path: its CUDA op runs a warp per (head,
+// query) over a serial page loop (src/backend/cuda/attention.cu:401-489),
+// and the CPU op folds one token at a time into an online softmax
+// (src/backend/cpu/attention.cpp:156-215). Here a chunk of S queries of one
+// query head attends causally over every cached page:
+//
+//   * CTA = 128 queries x 1 query head (grid ceil(S/128) x Hq), 4 warps; warp
+//     w owns TMEM lanes [32w, 32w+32), i.e. one query row per thread;
+//   * Q tile [128 x 128] and each KV tile (128 keys = 8 pages of 16 slots)
+//     arrive by TMA in the 128-byte-swizzled K-major layout: per page and
+//     per 64-dim half one box {64 dims, 1 head, 16 slots} of the pool's 3-D
+//     map; K and V tiles are double-buffered;
+//   * S = Q K^T: 8 tcgen05.mma (M128 N128 K16, bf16 -> fp32) into TMEM
+//     columns [0, 128), issued by one thread, completion by tcgen05.commit;
+//   * each thread loads its S row from TMEM, applies the causal / length
+//     mask, and updates an fp32 online softmax (log2 domain); the
+//     probabilities go to shared memory as bf16 in the swizzled K-major
+//     layout; O in TMEM columns [128, 256) is rescaled in place when the
+//     running max moves;
+//   * O += P V: 8 tcgen05.mma with V as an MN-major operand;
+//   * the epilogue divides by the row sum and stores fp32/bf16/fp16 rows.
+//
+// Keys past the cached length in the last tile are masked in S, and their V
+// rows are zeroed in shared memory (0 x NaN from stale slots would poison
+// the MMA). Every mbarrier wait is bounded (kErrTimeout).
+#include "device.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace gkv {
+namespace {
+
+constexpr int kBM = 128;  // queries per CTA
+constexpr int kBN = 128;  // keys per KV tile (8 pages)
+constexpr int kPagesPerTile = kBN / kPageSlots;
+constexpr uint32_t kHalf = 128 * 128;          // one 64-dim half of a 128-row tile: 16 KiB
+constexpr uint32_t kTile = 2 * kHalf;          // 32 KiB
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kOffQ + kTile;      // 2 stages
+constexpr uint32_t kOffV = kOffK + 2 * kTile;  // 2 stages
+constexpr uint32_t kOffP = kOffV + 2 * kTile;
+constexpr uint32_t kOffBar = kOffP + kTile;
+constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + barriers, TMEM slot, alignment slack
+constexpr uint32_t kTmemCols = 256;            // S: [0, 128), O: [128, 256)
+
+struct TcParams {
+    const int2* table;
+    void* out;
+    uint32_t* err;
+    int32_t out_dtype;
+    int32_t n_q_heads;
+    int32_t n_kv_heads;
+    int32_t seq_len;
+    int32_t total;
+    int32_t n_pages;
+    int32_t pool_pages;
+    int32_t causal;
+    float qscale;  // softmax scale * log2(e)
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(128, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                      const __grid_constant__ CUtensorMap v_map, const TcParams a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* bar_kv = bar_q + 1;  // [2]
+    uint64_t* bar_s = bar_q + 3;
+    uint64_t* bar_o = bar_q + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + 5);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int q0 = blockIdx.x * kBM;
+    const int hq = blockIdx.y;
+    const int G = a.n_q_heads / a.n_kv_heads;
+    const int h = hq / G;
+    const int S = a.seq_len;
+    const int first_q_abs = a.total - S + q0;
+    const int last_q_abs = min(a.total - 1, first_q_abs + kBM - 1);
+    const int kv_end = a.causal ? last_q_abs + 1 : a.total;
+    const int n_tiles = (kv_end + kBN - 1) / kBN;
+
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        mbar_init(bar_q, 1);
+        mbar_init(&bar_kv[0], 1);
+        mbar_init(&bar_kv[1], 1);
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        fence_mbar_init();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_s = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's lanes, S columns
+    const uint32_t t_o = t_s + 128;                              // O columns
+
+    const uint32_t sQ = smem_addr(smem + kOffQ);
+    const uint32_t sK = smem_addr(smem + kOffK);
+    const uint32_t sV = smem_addr(smem + kOffV);
+    const uint32_t sP = smem_addr(smem + kOffP);
+    const uint64_t pol = l2_policy_evict_first();
+
+    // Stage KV tile j into buffer (j & 1): 8 pages x 2 halves for K and V.
+    auto issue_kv = [&](int j) {
+        const int st = j & 1;
+        uint64_t* bar = &bar_kv[st];
+        mbar_arrive_expect_tx(bar, 2 * kTile);
+        for (int i = 0; i < kPagesPerTile; ++i) {
+            int lp = j * kPagesPerTile + i;
+            if (lp >= a.n_pages) lp = a.n_pages - 1;  // beyond the cache: rows are masked / zeroed
+            int2 e = a.table[lp];
+            if (e.x < 0 || e.x >= a.pool_pages || e.y < 0 || e.y >= a.pool_pages) {
+                atomicOr(a.err, kErrBadPage);
+                e = make_int2(0, 0);
+            }
+            for (int hf = 0; hf < 2; ++hf) {
+                tma_load_3d(smem + kOffK + st * kTile + hf * kHalf + i * 2048, &k_map, bar, hf * 64, h,
+                            e.x * kPageSlots, pol);
+                tma_load_3d(smem + kOffV + st * kTile + hf * kHalf + i * 2048, &v_map, bar, hf * 64, h,
+                            e.y * kPageSlots, pol);
+            }
+        }
+    };
+
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar_q, kTile);
+        tma_load_3d(smem + kOffQ, &q_map, bar_q, 0, q0, hq, pol);
+        tma_load_3d(smem + kOffQ + kHalf, &q_map, bar_q, 64, q0, hq, pol);
+        issue_kv(0);
+        if (n_tiles > 1) issue_kv(1);
+    }
+
+    constexpr uint32_t kIdescQK = tc::idesc_bf16_f32(128, 128, false, false);
+    constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, false, true);
+
+    const int r = tid;  // query row of this thread
+    const int q_abs = first_q_abs + r;
+    const int lim = a.causal ? min(q_abs, a.total - 1) : a.total - 1;  // last visible key
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+
+    // A wait that times out clears `ok`; later waits are then skipped, but
+    // every thread still reaches every __syncthreads, so nothing can hang.
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (ok && !mbar_wait_bounded(bar, parity)) ok = false;
+    };
+
+    for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        wait(&bar_kv[st], (j >> 1) & 1);
+        const int key0 = j * kBN;
+        // Zero V rows past the cache in this tile.
+        const int valid_rows = min(kBN, a.total - key0);
+        if (r >= valid_rows) {
+            uint4 z = make_uint4(0, 0, 0, 0);
+            uint4* v0 = reinterpret_cast<uint4*>(smem + kOffV + st * kTile + r * 128);
+            uint4* v1 = reinterpret_cast<uint4*>(smem + kOffV + st * kTile + kHalf + r * 128);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                v0[c] = z;
+                v1[c] = z;
+            }
+            fence_proxy_async_smem();
+        }
+        if (tid == 0) {
+            if (j == 0) wait(bar_q, 0);
+            tc::fence_after_sync();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+                const uint64_t da = tc::smem_desc_sw128(sQ + off, 16, 1024);
+                const uint64_t db = tc::smem_desc_sw128(sK + st * kTile + off, 16, 1024);
+                tc::mma_bf16(tmem, da, db, kIdescQK, kk > 0);
+            }
+            tc::commit(bar_s);
+        }
+        wait(bar_s, j & 1);
+        tc::fence_after_sync();
+
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc::ld32(t_s + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+        tc::wait_ld();
+
+        const int n_ok = max(0, min(kBN, lim - key0 + 1));
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+            const float v = c < n_ok ? s[c] * a.qscale : -INFINITY;
+            s[c] = v;
+            mx = fmaxf(mx, v);
+        }
+        const float m_new = fmaxf(m_run, mx);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = exp2_approx(m_run - m_use);
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+            const float p = exp2_approx(s[c] - m_use);
+            s[c] = p;
+            sum += p;
+        }
+        l_run = l_run * alpha + sum;
+        m_run = m_new;
+
+        if (j > 0) {
+            // The previous P.V must be done before P and O are touched.
+            wait(bar_o, (j - 1) & 1);
+            tc::fence_after_sync();
+            if (tid == 0 && j + 1 < n_tiles) issue_kv(j + 1);
+            if (__any_sync(0xFFFFFFFFu, alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float o[32];
+                    tc::ld32(t_o + c * 32, o);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tc::st32(t_o + c * 32, o);
+                }
+                tc::wait_st();
+            }
+        }
+
+        // P (bf16) into the swizzled K-major layout: row r, 16-byte chunk c of
+        // each 64-key half at position c ^ (r & 7).
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            uint4 w;
+            w.x = pack_bf16(s[c * 8 + 0], s[c * 8 + 1]);
+            w.y = pack_bf16(s[c * 8 + 2], s[c * 8 + 3]);
+            w.z = pack_bf16(s[c * 8 + 4], s[c * 8 + 5]);
+            w.w = pack_bf16(s[c * 8 + 6], s[c * 8 + 7]);
+            const int hf = c >> 3, cc = c & 7;
+            *reinterpret_cast<uint4*>(smem + kOffP + hf * kHalf + r * 128 + ((cc ^ (r & 7)) * 16)) = w;
+        }
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after_sync();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint64_t da = tc::smem_desc_sw128(sP + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                const uint64_t db = tc::smem_desc_sw128(sV + st * kTile + kk * 2048, kHalf, 1024);
+                tc::mma_bf16(tmem + 128, da, db, kIdescPV, j > 0 || kk > 0);
+            }
+            tc::commit(bar_o);
+        }
+    }
+
+    wait(bar_o, (n_tiles - 1) & 1);
+    tc::fence_after_sync();
+    const float inv = 1.f / l_run;
+    const int q = q0 + r;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tc::ld32(t_o + c * 32, o);  // warp-collective: executed even on the error path
+        tc::wait_ld();
+        if (ok && q < S) {
+            const size_t base = ((size_t)hq * S + q) * kHeadDim + c * 32;
+            if (a.out_dtype == 0) {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) store_out(a.out, base + i, o[i] * inv, a.out_dtype);
+            }
+        }
+    }
+    if (!ok) atomicOr(a.err, kErrTimeout);
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const CUtensorMap& k_map,
+                              const CUtensorMap& v_map, const int2* table, const PrefillLaunch& p, uint32_t* err,
+                              cudaStream_t stream) {
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64 || !(configured & (1ull << dev))) {
+        e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) configured |= 1ull << dev;
+    }
+    TcParams a;
+    a.table = table;
+    a.out = p.out;
+    a.err = err;
+    a.out_dtype = p.out_dtype;
+    a.n_q_heads = p.n_q_heads;
+    a.n_kv_heads = pool.n_kv_heads;
+    a.seq_len = p.seq_len;
+    a.total = p.total;
+    a.n_pages = p.n_pages;
+    a.pool_pages = pool.pool_pages;
+    a.causal = p.causal;
+    a.qscale = p.scale * 1.4426950408889634f;
+    dim3 grid((p.seq_len + kBM - 1) / kBM, p.n_q_heads);
+    prefill_tc_kernel<<<grid, 128, kSmemBytes, stream>>>(q_map, k_map, v_map, a);
+    return cudaGetLastError();
+}
+
+}  // namespace gkv

@@ -70,6 +70,9 @@ class Oracle:
         L.orc_paged_attention_f32.restype = None
         L.orc_paged_attention_f32_mt.argtypes = L.orc_paged_attention_f32.argtypes + [C.c_int32]
         L.orc_paged_attention_f32_mt.restype = None
+        L.orc_paged_attention_rows.argtypes = ([_vp, C.c_int32, _vp, _vp, _vp, _vp] + [C.c_int32] * 7 +
+                                               [C.c_float, C.c_int, _vp, C.c_int32, _vp, C.c_int32])
+        L.orc_paged_attention_rows.restype = None
         L.orc_bf16_from_f32.argtypes = [C.c_float]
         L.orc_bf16_from_f32.restype = C.c_uint16
         L.orc_round_bf16.argtypes = [_vp, _vp, C.c_size_t]
@@ -89,6 +92,20 @@ class Oracle:
             self.lib.orc_paged_attention_f32_mt(*args, int(threads))
         else:
             self.lib.orc_paged_attention_f32(*args)
+        return out
+
+    def paged_attention_rows(self, q, k_pool, v_pool, k_ids, v_ids, total, n_q_heads, n_kv_heads,
+                             seq_len, head_dim, scale, rows, causal=True, dtype=BF16, threads=1):
+        """Only the listed output rows (r = head * seq_len + query): fp32 [len(rows)][D]."""
+        q = np.ascontiguousarray(q)
+        k_ids = np.ascontiguousarray(k_ids, dtype=np.int32)
+        v_ids = np.ascontiguousarray(v_ids, dtype=np.int32)
+        rows = np.ascontiguousarray(rows, dtype=np.int32)
+        out = np.empty((len(rows), head_dim), dtype=np.float32)
+        self.lib.orc_paged_attention_rows(_ptr(q), dtype, _ptr(k_pool), _ptr(v_pool), _ptr(k_ids), _ptr(v_ids),
+                                          len(k_ids), total, n_q_heads, n_kv_heads, seq_len, head_dim,
+                                          n_q_heads // n_kv_heads, scale, int(bool(causal)), _ptr(rows),
+                                          len(rows), _ptr(out), int(threads))
         return out
 
     def round_bf16(self, x: np.ndarray) -> np.ndarray:

@@ -180,48 +180,68 @@ void orc_layer_append_kv(orc_layer* L, uint8_t* k_pool_base, uint8_t* v_pool_bas
 
 /* ---- attention: src/backend/cpu/attention.cpp:156-215 ------------------- */
 
-static void attend_rows(const uint8_t* q, int32_t dtype, const uint8_t* kb, const uint8_t* vb,
-                        const int32_t* k_ids, const int32_t* v_ids, int32_t n_pages,
-                        int32_t total, int32_t Hq, int32_t Hkv, int32_t S, int32_t D,
-                        int32_t groups, float scale, int causal, float* out, int32_t row0,
-                        int32_t row1) {
+/* One output row r = h * S + sq. The bf16 path converts Q once per row and
+ * each K/V element as it is used; the float operations and their order are
+ * exactly the reference loop's (the conversions are exact). */
+static void attend_one(const uint8_t* q, int32_t dtype, const uint8_t* kb, const uint8_t* vb,
+                       const int32_t* k_ids, const int32_t* v_ids, int32_t n_pages, int32_t total,
+                       int32_t Hkv, int32_t S, int32_t D, int32_t groups, float scale, int causal,
+                       int32_t r, float* orow, float* o, float* qf) {
     int32_t eb = elem_bytes(dtype);
     size_t page_elems = (size_t)ORC_PAGE_SLOTS * Hkv * D;
-    float* o = (float*)malloc(sizeof(float) * (size_t)D);
-    for (int32_t r = row0; r < row1; ++r) {
-        int32_t h = r / S, sq = r % S;
-        int32_t kvh = h / groups;
-        float m = -INFINITY, l = 0.0f;
-        for (int32_t d = 0; d < D; ++d) o[d] = 0.0f;
-        int32_t q_abs = total - S + sq;
-        int32_t limit = causal ? q_abs : total - 1;
-        const uint8_t* qrow = q + (((size_t)h * S + sq) * D) * eb;
-        for (int32_t blk = 0; blk < n_pages; ++blk) {
-            int32_t start = blk * ORC_PAGE_SLOTS;
-            int32_t end = start + ORC_PAGE_SLOTS < total ? start + ORC_PAGE_SLOTS : total;
-            if (start > limit) break;
-            const uint8_t* kp = kb + (size_t)k_ids[blk] * page_elems * eb;
-            const uint8_t* vp = vb + (size_t)v_ids[blk] * page_elems * eb;
-            for (int32_t s = 0; s < end - start; ++s) {
-                if (causal && start + s > q_abs) break;
-                size_t off = ((size_t)s * Hkv + kvh) * D;
-                float score = 0.0f;
-                for (int32_t d = 0; d < D; ++d)
-                    score += load_elem(qrow + (size_t)d * eb, dtype) *
-                             load_elem(kp + (off + d) * eb, dtype);
-                score *= scale;
-                float mp = m;
-                m = fmaxf(m, score);
-                float es = expf(score - m);
-                float ep = expf(mp - m);
-                for (int32_t d = 0; d < D; ++d)
-                    o[d] = o[d] * ep + es * load_elem(vp + (off + d) * eb, dtype);
-                l = l * ep + es;
+    int32_t h = r / S, sq = r % S;
+    int32_t kvh = h / groups;
+    float m = -INFINITY, l = 0.0f;
+    for (int32_t d = 0; d < D; ++d) o[d] = 0.0f;
+    int32_t q_abs = total - S + sq;
+    int32_t limit = causal ? q_abs : total - 1;
+    const uint8_t* qrow = q + (((size_t)h * S + sq) * D) * eb;
+    for (int32_t d = 0; d < D; ++d) qf[d] = load_elem(qrow + (size_t)d * eb, dtype);
+    for (int32_t blk = 0; blk < n_pages; ++blk) {
+        int32_t start = blk * ORC_PAGE_SLOTS;
+        int32_t end = start + ORC_PAGE_SLOTS < total ? start + ORC_PAGE_SLOTS : total;
+        if (start > limit) break;
+        const uint8_t* kp = kb + (size_t)k_ids[blk] * page_elems * eb;
+        const uint8_t* vp = vb + (size_t)v_ids[blk] * page_elems * eb;
+        for (int32_t s = 0; s < end - start; ++s) {
+            if (causal && start + s > q_abs) break;
+            size_t off = ((size_t)s * Hkv + kvh) * D;
+            float score = 0.0f;
+            if (dtype == ORC_BF16) {
+                const uint16_t* kr = (const uint16_t*)(kp + off * 2);
+                for (int32_t d = 0; d < D; ++d) score += qf[d] * orc_bf16_to_f32(kr[d]);
+            } else {
+                for (int32_t d = 0; d < D; ++d) score += qf[d] * load_elem(kp + (off + d) * eb, dtype);
             }
+            score *= scale;
+            float mp = m;
+            m = fmaxf(m, score);
+            float es = expf(score - m);
+            float ep = expf(mp - m);
+            if (dtype == ORC_BF16) {
+                const uint16_t* vr = (const uint16_t*)(vp + off * 2);
+                for (int32_t d = 0; d < D; ++d) o[d] = o[d] * ep + es * orc_bf16_to_f32(vr[d]);
+            } else {
+                for (int32_t d = 0; d < D; ++d) o[d] = o[d] * ep + es * load_elem(vp + (off + d) * eb, dtype);
+            }
+            l = l * ep + es;
         }
-        float inv = 1.0f / l;
-        float* orow = out + ((size_t)h * S + sq) * D;
-        for (int32_t d = 0; d < D; ++d) orow[d] = o[d] * inv;
+    }
+    float inv = 1.0f / l;
+    for (int32_t d = 0; d < D; ++d) orow[d] = o[d] * inv;
+}
+
+/* Rows rows[i0..i1) (or r = i0..i1 when rows is NULL) into out[i][D]. */
+static void attend_rows(const uint8_t* q, int32_t dtype, const uint8_t* kb, const uint8_t* vb,
+                        const int32_t* k_ids, const int32_t* v_ids, int32_t n_pages, int32_t total,
+                        int32_t Hq, int32_t Hkv, int32_t S, int32_t D, int32_t groups, float scale,
+                        int causal, float* out, int32_t i0, int32_t i1, const int32_t* rows) {
+    (void)Hq;
+    float* o = (float*)malloc(sizeof(float) * (size_t)D * 2);
+    for (int32_t i = i0; i < i1; ++i) {
+        int32_t r = rows ? rows[i] : i;
+        attend_one(q, dtype, kb, vb, k_ids, v_ids, n_pages, total, Hkv, S, D, groups, scale, causal, r,
+                   out + (size_t)i * D, o, o + D);
     }
     free(o);
 }
@@ -231,12 +251,12 @@ void orc_paged_attention_f32(const uint8_t* q, int32_t dtype, const uint8_t* kb,
                              int32_t n_pages, int32_t total, int32_t Hq, int32_t Hkv, int32_t S,
                              int32_t D, int32_t groups, float scale, int causal, float* out) {
     attend_rows(q, dtype, kb, vb, k_ids, v_ids, n_pages, total, Hq, Hkv, S, D, groups, scale,
-                causal, out, 0, Hq * S);
+                causal, out, 0, Hq * S, NULL);
 }
 
 typedef struct {
     const uint8_t *q, *kb, *vb;
-    const int32_t *k_ids, *v_ids;
+    const int32_t *k_ids, *v_ids, *rows;
     int32_t dtype, n_pages, total, Hq, Hkv, S, D, groups, causal, row0, row1;
     float scale;
     float* out;
@@ -245,8 +265,29 @@ typedef struct {
 static void* orc_job_run(void* a) {
     orc_job* j = (orc_job*)a;
     attend_rows(j->q, j->dtype, j->kb, j->vb, j->k_ids, j->v_ids, j->n_pages, j->total, j->Hq,
-                j->Hkv, j->S, j->D, j->groups, j->scale, j->causal, j->out, j->row0, j->row1);
+                j->Hkv, j->S, j->D, j->groups, j->scale, j->causal, j->out, j->row0, j->row1, j->rows);
     return NULL;
+}
+
+static void run_threads(const uint8_t* q, int32_t dtype, const uint8_t* kb, const uint8_t* vb,
+                        const int32_t* k_ids, const int32_t* v_ids, int32_t n_pages, int32_t total,
+                        int32_t Hq, int32_t Hkv, int32_t S, int32_t D, int32_t groups, float scale,
+                        int causal, float* out, int32_t n_rows, const int32_t* rows,
+                        int32_t n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > n_rows) n_threads = n_rows > 0 ? n_rows : 1;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)n_threads);
+    orc_job* jobs = (orc_job*)malloc(sizeof(orc_job) * (size_t)n_threads);
+    for (int32_t t = 0; t < n_threads; ++t) {
+        orc_job j = {q, kb, vb, k_ids, v_ids, rows, dtype, n_pages, total, Hq, Hkv, S, D, groups,
+                     causal, (int32_t)((int64_t)n_rows * t / n_threads),
+                     (int32_t)((int64_t)n_rows * (t + 1) / n_threads), scale, out};
+        jobs[t] = j;
+        pthread_create(&th[t], NULL, orc_job_run, &jobs[t]);
+    }
+    for (int32_t t = 0; t < n_threads; ++t) pthread_join(th[t], NULL);
+    free(th);
+    free(jobs);
 }
 
 void orc_paged_attention_f32_mt(const uint8_t* q, int32_t dtype, const uint8_t* kb,
@@ -254,19 +295,16 @@ void orc_paged_attention_f32_mt(const uint8_t* q, int32_t dtype, const uint8_t* 
                                 int32_t n_pages, int32_t total, int32_t Hq, int32_t Hkv,
                                 int32_t S, int32_t D, int32_t groups, float scale, int causal,
                                 float* out, int32_t n_threads) {
-    int32_t rows = Hq * S;
-    if (n_threads < 1) n_threads = 1;
-    if (n_threads > rows) n_threads = rows;
-    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)n_threads);
-    orc_job* jobs = (orc_job*)malloc(sizeof(orc_job) * (size_t)n_threads);
-    for (int32_t t = 0; t < n_threads; ++t) {
-        orc_job j = {q, kb, vb, k_ids, v_ids, dtype, n_pages, total, Hq, Hkv, S, D, groups,
-                     causal, (int32_t)((int64_t)rows * t / n_threads),
-                     (int32_t)((int64_t)rows * (t + 1) / n_threads), scale, out};
-        jobs[t] = j;
-        pthread_create(&th[t], NULL, orc_job_run, &jobs[t]);
-    }
-    for (int32_t t = 0; t < n_threads; ++t) pthread_join(th[t], NULL);
-    free(th);
-    free(jobs);
+    run_threads(q, dtype, kb, vb, k_ids, v_ids, n_pages, total, Hq, Hkv, S, D, groups, scale,
+                causal, out, Hq * S, NULL, n_threads);
+}
+
+void orc_paged_attention_rows(const uint8_t* q, int32_t dtype, const uint8_t* kb,
+                              const uint8_t* vb, const int32_t* k_ids, const int32_t* v_ids,
+                              int32_t n_pages, int32_t total, int32_t Hq, int32_t Hkv, int32_t S,
+                              int32_t D, int32_t groups, float scale, int causal,
+                              const int32_t* rows, int32_t n_rows, float* out,
+                              int32_t n_threads) {
+    run_threads(q, dtype, kb, vb, k_ids, v_ids, n_pages, total, Hq, Hkv, S, D, groups, scale,
+                causal, out, n_rows, rows, n_threads);
 }

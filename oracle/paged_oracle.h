@@ -96,6 +96,14 @@ void orc_paged_attention_f32_mt(const uint8_t* q, int32_t dtype, const uint8_t* 
                                 int32_t head_dim, int32_t n_kv_groups, float scale, int causal,
                                 float* out, int32_t n_threads);
 
+/* Only the output rows listed (row r = head * S + query), out[i][D]. */
+void orc_paged_attention_rows(const uint8_t* q, int32_t dtype, const uint8_t* k_pool_base,
+                              const uint8_t* v_pool_base, const int32_t* k_ids,
+                              const int32_t* v_ids, int32_t n_pages, int32_t total_cached,
+                              int32_t n_q_heads, int32_t n_kv_heads, int32_t seq_len,
+                              int32_t head_dim, int32_t n_kv_groups, float scale, int causal,
+                              const int32_t* rows, int32_t n_rows, float* out, int32_t n_threads);
+
 /* Round an fp32 buffer to the reference's bf16 (RNE, subnormals to signed 0). */
 void orc_round_bf16(const float* in, uint16_t* out, size_t n);
 

@@ -259,3 +259,69 @@ def test_append_only_bit_exact():
     assert np.array_equal(bits_of(vp).reshape(o_vp.shape), o_vp)
     assert m.get_layer(0).num_cached == o_n
     assert m.device_table(0)[0] == o_k.tolist()
+
+
+def test_config4_chunked_prefill_qwen3_1p7b():
+    """Config 4: an 8192-token prompt in 16 chunks of 512 (Hq 16, Hkv 8),
+    each chunk appended into 16-token pages and attended causally over all
+    prior pages on the tensor cores. Every chunk's pool bytes are bit-exact
+    against the restated appender; 48 output rows per chunk (first, last and
+    random rows of random heads) are checked against the oracle."""
+    from genllm_b200.synth import randn_bf16
+    from oracle.oracle import OraclePool
+    hq, hkv, d, chunk, n_chunks = 16, 8, 128, 512, 16
+    pool_pages = chunk * n_chunks // 16 + 8
+    rng = np.random.default_rng(4)
+    m = PagedAttentionManager(0)
+    m.init_layer(0, hkv, d)
+    m.reserve_layer(0, pool_pages)
+    op = OraclePool(pool_pages, ORC)
+    kp = np.zeros((pool_pages, 16, hkv, d), np.uint16)
+    vp = np.zeros((pool_pages, 16, hkv, d), np.uint16)
+    scale = 1 / np.sqrt(d)
+    for c in range(n_chunks):
+        q = randn_bf16(rng, (hq, chunk, d))
+        kn = randn_bf16(rng, (hkv, chunk, d))
+        vn = randn_bf16(rng, (hkv, chunk, d))
+        out = torch.empty((1, hq, chunk, d), dtype=torch.float32, device="cuda")
+        paged_attention(m, 0, to_dev_bf16(q, "cuda").view(1, hq, chunk, d),
+                        to_dev_bf16(kn, "cuda").view(1, hkv, chunk, d),
+                        to_dev_bf16(vn, "cuda").view(1, hkv, chunk, d), out=out, scale=scale)
+        op.append_kv(kp, vp, kn, vn, hkv, chunk, d)
+        k_ids, v_ids = op.table()
+        rows = np.concatenate([[0, chunk - 1, hq * chunk - 1], rng.integers(0, hq * chunk, 45)]).astype(np.int32)
+        want = ORC.paged_attention_rows(q, kp, vp, k_ids, v_ids, op.num_cached, hq, hkv, chunk, d, scale, rows,
+                                        threads=min(NPROC, 32))
+        torch.cuda.synchronize()
+        got = out[0].reshape(hq * chunk, d).cpu().numpy()[rows]
+        assert_close(got, want, f"chunk {c}")
+    gk, gv = m.pool_tensors(0)
+    assert np.array_equal(bits_of(gk), kp) and np.array_equal(bits_of(gv), vp)
+    assert m.check_device_errors(0) == 0
+
+
+def test_prefill_kernels_agree_simt_subprocess():
+    """The CUDA-core prefill kernel (GKV_PREFILL_KERNEL=simt) is an
+    independent second implementation; both must match the oracle."""
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+        "from test_gpu_parity import check_case\n"
+        "from genllm_b200.synth import fragmented_case\n"
+        "check_case(fragmented_case(401, 16, 8, 128, 70, 30, n_new=130), True)\n"
+        "check_case(fragmented_case(402, 8, 2, 128, 5, 20, n_new=77), False)\n"
+        "print('simt ok')\n" % (os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                os.path.dirname(os.path.abspath(__file__))))
+    env = dict(os.environ, GKV_PREFILL_KERNEL="simt")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "simt ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("n_prior,n_new,causal", [(0, 128, True), (1, 255, True), (127, 129, False),
+                                                  (300, 384, True), (2000, 130, True)])
+def test_prefill_tile_edges(n_prior, n_new, causal):
+    """Query tiles of exactly / one past 128 rows, KV tiles ending mid-page."""
+    case = fragmented_case(500 + n_new, 16, 8, 128, n_prior, (n_prior + n_new) // 16 + 3, n_new=n_new,
+                           poison_unused=True)
+    check_case(case, causal)
