@@ -43,8 +43,10 @@ constexpr uint32_t kTile = 2 * kTileHalf;            // one (page, head) K or V 
 constexpr uint32_t kStageKV = kConsumerWarps * kTile;  // 32 KiB of K (or V) per stage
 constexpr uint32_t kStageBytes = 2 * kStageKV;        // 64 KiB
 constexpr uint32_t kOffBar = kStages * kStageBytes;
-constexpr uint32_t kOffP = kOffBar + 2 * kStages * 8;            // per-warp P buffers
-constexpr uint32_t kSmemBytes = kOffP + kConsumerWarps * 256 + 1024;  // + alignment slack
+constexpr uint32_t kOffP = kOffBar + 2 * kStages * 8;            // per-warp P^T hi/lo buffers
+constexpr int kMaxSplitPages = 1024;                              // page ids cached per CTA
+constexpr uint32_t kOffIds = kOffP + kConsumerWarps * 512;
+constexpr uint32_t kSmemBytes = kOffIds + kMaxSplitPages * 8 + 1024;  // + alignment slack
 static_assert(kConsumerWarps * 8 * (kHeadDim + 2) * 4 <= kStages * kStageBytes, "merge buffers fit");
 
 struct DecodeParams {
@@ -108,11 +110,6 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
                         const DecodeParams a) {
@@ -135,6 +132,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // from its parameters; later launches read the table).
     if (split == 0 && (int)threadIdx.x < a.new_n) a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
 
+    // This split's page ids, bounds-checked once, into shared memory (a bad id
+    // becomes {-1, -1}: loaded as page 0, skipped by the consumer).
+    int2* ids = reinterpret_cast<int2*>(smem + kOffIds);
+    for (int i = threadIdx.x; i < p1 - p0; i += kThreads) {
+        int2 e = page_entry(a, p0 + i);
+        if (!entry_ok(a, e)) {
+            atomicOr(a.err, kErrBadPage);
+            e = make_int2(-1, -1);
+        }
+        ids[i] = e;
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
@@ -159,11 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 mbar_arrive_expect_tx(&full[st], (uint32_t)(np * Hkv) * 2u * kTile);
                 for (int pi = 0; pi < np; ++pi) {
-                    int2 e = page_entry(a, p0 + i * P + pi);
-                    if (!entry_ok(a, e)) {
-                        atomicOr(a.err, kErrBadPage);
-                        e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
-                    }
+                    int2 e = ids[i * P + pi];
+                    if (e.x < 0) e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
                     for (int h = 0; h < Hkv; ++h) {
                         const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
                         for (int hf = 0; hf < 2; ++hf) {
@@ -181,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool active = pslot < P;
         const int g = lane >> 2;                // fragment row group
         const int t = lane & 3;                 // fragment column pair
-        uint8_t* pbuf = smem + kOffP + warp * 256;  // P^T staging: [8 heads][16 slots] bf16
+        uint8_t* pbuf = smem + kOffP + warp * 512;  // P^T staging: hi and lo [8 heads][16 slots] bf16
 
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
         uint32_t qb[8][2];
@@ -210,8 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok_wait && lane == 0) atomicOr(a.err, kErrTimeout);
             const int lp = p0 + i * P + pslot;
             const bool have = active && lp < p1 && ok_wait;
-            int2 e = have ? page_entry(a, lp) : make_int2(0, 0);
-            const bool use = have && entry_ok(a, e);
+            const int2 e = have ? ids[lp - p0] : make_int2(-1, -1);
+            const bool use = have && e.x >= 0;
             if (use) {
                 uint8_t* kt = smem + st * kStageBytes + (uint32_t)(pslot * Hkv + head) * kTile;
                 uint8_t* vt = kt + kStageKV;
@@ -239,14 +244,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
 
                 // S^T[slot][head] = K Q^T
-                float s[4] = {0.f, 0.f, 0.f, 0.f};
+                // Two independent accumulation chains (even / odd k-steps).
+                float s[4] = {0.f, 0.f, 0.f, 0.f}, s_odd[4] = {0.f, 0.f, 0.f, 0.f};
                 const uint32_t ks = smem_addr(kt);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    uint32_t a0, a1, a2, a3;
+                for (int kk = 0; kk < 8; kk += 2) {
+                    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
                     ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+                    ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + 2 + (mi >> 1)), b0, b1, b2, b3);
                     mma_bf16_16816(s, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+                    mma_bf16_16816(s_odd, b0, b1, b2, b3, qb[kk + 1][0], qb[kk + 1][1]);
                 }
+#pragma unroll
+                for (int i2 = 0; i2 < 4; ++i2) s[i2] += s_odd[i2];
                 // s[0]: (slot g, head 2t) s[1]: (g, 2t+1) s[2]: (g+8, 2t) s[3]: (g+8, 2t+1)
                 const bool v_lo = g < nvalid, v_hi = g + 8 < nvalid;
                 const float s0 = v_lo ? s[0] * a.qscale : -INFINITY;
@@ -280,22 +290,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc[mt][2] *= al0;
                     acc[mt][3] *= al1;
                 }
-                // P^T staging: pbuf[head][slot] (bf16), then B fragments of O^T += V^T P^T.
+                // P^T staging as bf16 hi + lo (P = hi + lo to ~2^-17 relative), so the
+                // PV products keep fp32-level accuracy: pbuf[0|1][head][slot].
                 uint16_t* pb = reinterpret_cast<uint16_t*>(pbuf);
-                const uint32_t w01 = pack_bf16x2(p0v, p1v), w23 = pack_bf16x2(p2v, p3v);
-                pb[(2 * t) * 16 + g] = (uint16_t)(w01 & 0xFFFFu);
-                pb[(2 * t + 1) * 16 + g] = (uint16_t)(w01 >> 16);
-                pb[(2 * t) * 16 + g + 8] = (uint16_t)(w23 & 0xFFFFu);
-                pb[(2 * t + 1) * 16 + g + 8] = (uint16_t)(w23 >> 16);
+                {
+                    const float pv[4] = {p0v, p1v, p2v, p3v};
+                    const int hh[4] = {2 * t, 2 * t + 1, 2 * t, 2 * t + 1};
+                    const int ss[4] = {g, g, g + 8, g + 8};
+#pragma unroll
+                    for (int i2 = 0; i2 < 4; ++i2) {
+                        const __nv_bfloat16 hi = __float2bfloat16_rn(pv[i2]);
+                        const __nv_bfloat16 lo = __float2bfloat16_rn(pv[i2] - __bfloat162float(hi));
+                        pb[hh[i2] * 16 + ss[i2]] = __bfloat16_as_ushort(hi);
+                        pb[128 + hh[i2] * 16 + ss[i2]] = __bfloat16_as_ushort(lo);
+                    }
+                }
                 __syncwarp();
-                const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(pb + g * 16 + 2 * t);
-                const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(pb + g * 16 + 2 * t + 8);
+                const uint32_t ph0 = *reinterpret_cast<const uint32_t*>(pb + g * 16 + 2 * t);
+                const uint32_t ph1 = *reinterpret_cast<const uint32_t*>(pb + g * 16 + 2 * t + 8);
+                const uint32_t pl0 = *reinterpret_cast<const uint32_t*>(pb + 128 + g * 16 + 2 * t);
+                const uint32_t pl1 = *reinterpret_cast<const uint32_t*>(pb + 128 + g * 16 + 2 * t + 8);
                 const uint32_t vs = smem_addr(vt);
 #pragma unroll
                 for (int mt = 0; mt < 8; ++mt) {
                     uint32_t a0, a1, a2, a3;
                     ldsm_x4_t(vs + tile_off(lr + (mi >> 1) * 8, 2 * mt + (mi & 1)), a0, a1, a2, a3);
-                    mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+                    mma_bf16_16816(acc[mt], a0, a1, a2, a3, ph0, ph1);
+                    mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
                 }
                 fence_proxy_async_smem();  // generic writes above precede the next TMA into this stage
             }
@@ -362,46 +383,55 @@ struct CombineParams {
     int32_t n_splits;
 };
 
-// One CTA per query head, one thread per dim: merge the splits' (m, l, acc).
-__global__ void __launch_bounds__(kHeadDim) paged_decode_combine_kernel(const CombineParams c) {
+constexpr int kCombineWarps = 8;
+constexpr int kCombineDims = 32;  // dims per CTA (one per lane)
+
+// Grid (Hq, 128 / 32): warp w of a CTA folds splits w, w + 8, ... for the
+// CTA's 32 dims (one per lane, 128-byte coalesced rows), then the 8 warps
+// merge through shared memory.
+__global__ void __launch_bounds__(kCombineWarps * 32) paged_decode_combine_kernel(const CombineParams c) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
-    const int hq = blockIdx.x, d = threadIdx.x;
-    __shared__ float s_f[1024];
-    __shared__ float s_m[kHeadDim / 32];
-    __shared__ float s_l[kHeadDim / 32];
-    __shared__ float s_inv;
+    const int hq = blockIdx.x;
+    const int d = blockIdx.y * kCombineDims + (threadIdx.x & 31);
+    const int w = threadIdx.x >> 5;
+    __shared__ float s_m[kCombineWarps], s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims];
+    // Global max of the split maxima (every warp computes it).
     float M = -INFINITY;
-    for (int s = threadIdx.x; s < c.n_splits; s += kHeadDim) M = fmaxf(M, c.part_ml[(size_t)s * c.n_q_heads + hq].x);
+    for (int s = threadIdx.x & 31; s < c.n_splits; s += 32) M = fmaxf(M, c.part_ml[(size_t)s * c.n_q_heads + hq].x);
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, m));
-    if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = M;
-    __syncthreads();
-    M = s_m[0];
-    for (int w = 1; w < kHeadDim / 32; ++w) M = fmaxf(M, s_m[w]);
     const float Ms = M == -INFINITY ? 0.f : M;
-    float L = 0.f;
-    for (int s = threadIdx.x; s < c.n_splits; s += kHeadDim) {
-        const float2 ml = c.part_ml[(size_t)s * c.n_q_heads + hq];
-        const float f = exp2_approx(ml.x - Ms);
-        if (s < 1024) s_f[s] = f;
-        L = fmaf(ml.y, f, L);
+    float L = 0.f, A0 = 0.f, A1 = 0.f;
+    int s = w;
+    for (; s + kCombineWarps < c.n_splits; s += 2 * kCombineWarps) {
+        const float2 ml0 = c.part_ml[(size_t)s * c.n_q_heads + hq];
+        const float2 ml1 = c.part_ml[(size_t)(s + kCombineWarps) * c.n_q_heads + hq];
+        const float a0 = c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d];
+        const float a1 = c.part_acc[((size_t)(s + kCombineWarps) * c.n_q_heads + hq) * kHeadDim + d];
+        const float f0 = exp2_approx(ml0.x - Ms), f1 = exp2_approx(ml1.x - Ms);
+        L = fmaf(ml0.y, f0, fmaf(ml1.y, f1, L));
+        A0 = fmaf(a0, f0, A0);
+        A1 = fmaf(a1, f1, A1);
     }
+    if (s < c.n_splits) {
+        const float2 ml0 = c.part_ml[(size_t)s * c.n_q_heads + hq];
+        const float f0 = exp2_approx(ml0.x - Ms);
+        L = fmaf(ml0.y, f0, L);
+        A0 = fmaf(c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d], f0, A0);
+    }
+    if ((threadIdx.x & 31) == 0) s_l[w] = L;
+    s_a[w][threadIdx.x & 31] = A0 + A1;
+    __syncthreads();
+    if (w == 0) {
+        float Lt = 0.f, At = 0.f;
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, m);
-    if ((threadIdx.x & 31) == 0) s_l[threadIdx.x >> 5] = L;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float tot = 0.f;
-        for (int w = 0; w < kHeadDim / 32; ++w) tot += s_l[w];
-        s_inv = 1.f / tot;
+        for (int k = 0; k < kCombineWarps; ++k) {
+            Lt += s_l[k];
+            At += s_a[k][threadIdx.x];
+        }
+        store_out(c.out, (size_t)hq * kHeadDim + d, At / Lt, c.out_dtype);
     }
-    __syncthreads();
-    float A = 0.f;
-    for (int s = 0; s < c.n_splits; ++s) {
-        const float f = s < 1024 ? s_f[s] : exp2_approx(c.part_ml[(size_t)s * c.n_q_heads + hq].x - Ms);
-        A = fmaf(c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d], f, A);
-    }
-    store_out(c.out, (size_t)hq * kHeadDim + d, A * s_inv, c.out_dtype);
+    (void)s_m;
 }
 
 }  // namespace
@@ -449,7 +479,12 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     if (n_splits > n_stages_total) n_splits = n_stages_total;
     if (n_splits * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / d.n_q_heads;
     if (n_splits < 1) n_splits = 1;
-    const int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
+    int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
+    if (stages_per_split * P > kMaxSplitPages) {  // very long contexts: more splits than SMs
+        stages_per_split = kMaxSplitPages / P;
+        n_splits = (n_stages_total + stages_per_split - 1) / stages_per_split;
+        if (n_splits * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
+    }
     p.pages_per_split = stages_per_split * P;
     n_splits = (d.n_pages + p.pages_per_split - 1) / p.pages_per_split;
 
@@ -459,8 +494,8 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
 
     CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(d.n_q_heads);
-    cfg.blockDim = dim3(kHeadDim);
+    cfg.gridDim = dim3(d.n_q_heads, kHeadDim / kCombineDims);
+    cfg.blockDim = dim3(kCombineWarps * 32);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

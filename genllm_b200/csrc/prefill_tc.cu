@@ -20,7 +20,8 @@
 //     probabilities go to shared memory as bf16 in the swizzled K-major
 //     layout; O in TMEM columns [128, 256) is rescaled in place when the
 //     running max moves;
-//   * O += P V: 8 tcgen05.mma with V as an MN-major operand;
+//   * O += P V: 16 tcgen05.mma with V as an MN-major operand — P enters as
+//     bf16 hi + lo terms so that the products keep fp32-level accuracy;
 //   * the epilogue divides by the row sum and stores fp32/bf16/fp16 rows.
 //
 // Keys past the cached length in the last tile are masked in S, and their V
@@ -41,8 +42,9 @@ constexpr uint32_t kTile = 2 * kHalf;          // 32 KiB
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kTile;      // 2 stages
 constexpr uint32_t kOffV = kOffK + 2 * kTile;  // 2 stages
-constexpr uint32_t kOffP = kOffV + 2 * kTile;
-constexpr uint32_t kOffBar = kOffP + kTile;
+constexpr uint32_t kOffP = kOffV + 2 * kTile;   // P as bf16 hi part
+constexpr uint32_t kOffPlo = kOffP + kTile;     // and lo part (P - hi), for fp32-level PV accuracy
+constexpr uint32_t kOffBar = kOffPlo + kTile;
 constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + barriers, TMEM slot, alignment slack
 constexpr uint32_t kTmemCols = 256;            // S: [0, 128), O: [128, 256)
 
@@ -60,11 +62,6 @@ struct TcParams {
     int32_t causal;
     float qscale;  // softmax scale * log2(e)
 };
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-}
 
 __global__ void __launch_bounds__(128, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
@@ -112,6 +109,7 @@ __global__ void __launch_bounds__(128, 1)
     const uint32_t sK = smem_addr(smem + kOffK);
     const uint32_t sV = smem_addr(smem + kOffV);
     const uint32_t sP = smem_addr(smem + kOffP);
+    const uint32_t sPlo = smem_addr(smem + kOffPlo);
     const uint64_t pol = l2_policy_evict_first();
 
     // Stage KV tile j into buffer (j & 1): 8 pages x 2 halves for K and V.
@@ -236,17 +234,26 @@ __global__ void __launch_bounds__(128, 1)
             }
         }
 
-        // P (bf16) into the swizzled K-major layout: row r, 16-byte chunk c of
-        // each 64-key half at position c ^ (r & 7).
+        // P into the swizzled K-major layout (row r, 16-byte chunk c of each
+        // 64-key half at position c ^ (r & 7)) as two bf16 terms, hi = bf16(P)
+        // and lo = bf16(P - hi): P.V = hi.V + lo.V keeps fp32-level accuracy
+        // where a single bf16 P would lose 2^-9 relative per probability.
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-            uint4 w;
-            w.x = pack_bf16(s[c * 8 + 0], s[c * 8 + 1]);
-            w.y = pack_bf16(s[c * 8 + 2], s[c * 8 + 3]);
-            w.z = pack_bf16(s[c * 8 + 4], s[c * 8 + 5]);
-            w.w = pack_bf16(s[c * 8 + 6], s[c * 8 + 7]);
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float x0 = s[c * 8 + 2 * i], x1 = s[c * 8 + 2 * i + 1];
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+                const float2 hf2 = __bfloat1622float2(h2);
+                const __nv_bfloat162 l2 = __floats2bfloat162_rn(x0 - hf2.x, x1 - hf2.y);
+                hw[i] = *reinterpret_cast<const uint32_t*>(&h2);
+                lw[i] = *reinterpret_cast<const uint32_t*>(&l2);
+            }
             const int hf = c >> 3, cc = c & 7;
-            *reinterpret_cast<uint4*>(smem + kOffP + hf * kHalf + r * 128 + ((cc ^ (r & 7)) * 16)) = w;
+            const uint32_t off = hf * kHalf + r * 128 + ((cc ^ (r & 7)) * 16);
+            *reinterpret_cast<uint4*>(smem + kOffP + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(smem + kOffPlo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
         fence_proxy_async_smem();
         tc::fence_before_sync();
@@ -255,9 +262,10 @@ __global__ void __launch_bounds__(128, 1)
             tc::fence_after_sync();
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
-                const uint64_t da = tc::smem_desc_sw128(sP + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                const uint32_t po = (kk >> 2) * kHalf + (kk & 3) * 32;
                 const uint64_t db = tc::smem_desc_sw128(sV + st * kTile + kk * 2048, kHalf, 1024);
-                tc::mma_bf16(tmem + 128, da, db, kIdescPV, j > 0 || kk > 0);
+                tc::mma_bf16(tmem + 128, tc::smem_desc_sw128(sP + po, 16, 1024), db, kIdescPV, j > 0 || kk > 0);
+                tc::mma_bf16(tmem + 128, tc::smem_desc_sw128(sPlo + po, 16, 1024), db, kIdescPV, true);
             }
             tc::commit(bar_o);
         }

@@ -114,9 +114,11 @@ def test_multi_step_decode_sequence():
         L = m.get_layer(0)
         assert [e.k_block_id for e in L.page_table] == k_ids.tolist()
     gk, gv = m.pool_tensors(0)
-    used = sorted(set(k_ids.tolist()))
-    assert np.array_equal(bits_of(gk)[used], kp[used])
-    assert np.array_equal(bits_of(gv)[used], vp[used])
+    gkb, gvb = bits_of(gk), bits_of(gv)
+    for pos in range(op.num_cached):  # every written row, bit for bit
+        lp, slot = divmod(pos, 16)
+        assert np.array_equal(gkb[k_ids[lp], slot], kp[k_ids[lp], slot])
+        assert np.array_equal(gvb[v_ids[lp], slot], vp[v_ids[lp], slot])
 
 
 def test_reset_then_reuse_lifo():
