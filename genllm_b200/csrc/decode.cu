@@ -29,6 +29,8 @@
 //
 // Page ids are bounds-checked (a bad id is skipped and sets kErrBadPage);
 // every mbarrier wait is bounded (kErrTimeout).
+#include <cstdlib>
+
 #include "device.cuh"
 #include "kernels.h"
 
@@ -132,6 +134,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // from its parameters; later launches read the table).
     if (split == 0 && (int)threadIdx.x < a.new_n) a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
 
+    // Programmatic dependent launch: the split-combine kernel that follows may
+    // be scheduled now (it waits for this grid's completion itself).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
     // This split's page ids, bounds-checked once, into shared memory (a bad id
     // becomes {-1, -1}: loaded as page 0, skipped by the consumer).
     int2* ids = reinterpret_cast<int2*>(smem + kOffIds);
@@ -188,6 +194,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = lane & 3;                 // fragment column pair
         uint8_t* pbuf = smem + kOffP + warp * 512;  // P^T staging: hi and lo [8 heads][16 slots] bf16
 
+        // This launch may overlap the tail of the previous kernel on the stream
+        // (programmatic dependent launch): the page stream above reads only
+        // cached pages, but Q and the new K/V row are that kernel's outputs.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
         uint32_t qb[8][2];
         {
@@ -370,8 +380,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (d == 0) a.part_ml[row] = make_float2(M, L);
         }
     }
-    // Let the combine kernel (programmatic dependent launch) start its prologue.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 struct CombineParams {
@@ -384,54 +392,80 @@ struct CombineParams {
 };
 
 constexpr int kCombineWarps = 8;
+constexpr int kMaxSplits = 160;  // = kCombineWarps * splits held per warp in the combine
 constexpr int kCombineDims = 32;  // dims per CTA (one per lane)
 
 // Grid (Hq, 128 / 32): warp w of a CTA folds splits w, w + 8, ... for the
 // CTA's 32 dims (one per lane, 128-byte coalesced rows), then the 8 warps
 // merge through shared memory.
-__global__ void __launch_bounds__(kCombineWarps * 32) paged_decode_combine_kernel(const CombineParams c) {
+__global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_kernel(const CombineParams c) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int hq = blockIdx.x;
-    const int d = blockIdx.y * kCombineDims + (threadIdx.x & 31);
+    const int lane = threadIdx.x & 31;
+    const int d = blockIdx.y * kCombineDims + lane;
     const int w = threadIdx.x >> 5;
-    __shared__ float s_m[kCombineWarps], s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims];
-    // Global max of the split maxima (every warp computes it).
+    constexpr int kBatch = 10;  // splits per warp in flight at once; 2 batches (n_splits <= 160)
+    __shared__ float s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims], s_m[kCombineWarps];
+    // Pass 1: the global max over split maxima (loads issued together).
     float M = -INFINITY;
-    for (int s = threadIdx.x & 31; s < c.n_splits; s += 32) M = fmaxf(M, c.part_ml[(size_t)s * c.n_q_heads + hq].x);
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, m));
+    for (int b = 0; b < 2; ++b) {
+        float mx[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const int s = w + (b * kBatch + i) * kCombineWarps;
+            mx[i] = s < c.n_splits ? c.part_ml[(size_t)s * c.n_q_heads + hq].x : -INFINITY;
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) M = fmaxf(M, mx[i]);
+    }
+    if (lane == 0) s_m[w] = M;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kCombineWarps; ++k) M = fmaxf(M, s_m[k]);
     const float Ms = M == -INFINITY ? 0.f : M;
-    float L = 0.f, A0 = 0.f, A1 = 0.f;
-    int s = w;
-    for (; s + kCombineWarps < c.n_splits; s += 2 * kCombineWarps) {
-        const float2 ml0 = c.part_ml[(size_t)s * c.n_q_heads + hq];
-        const float2 ml1 = c.part_ml[(size_t)(s + kCombineWarps) * c.n_q_heads + hq];
-        const float a0 = c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d];
-        const float a1 = c.part_acc[((size_t)(s + kCombineWarps) * c.n_q_heads + hq) * kHeadDim + d];
-        const float f0 = exp2_approx(ml0.x - Ms), f1 = exp2_approx(ml1.x - Ms);
-        L = fmaf(ml0.y, f0, fmaf(ml1.y, f1, L));
-        A0 = fmaf(a0, f0, A0);
-        A1 = fmaf(a1, f1, A1);
+    // Pass 2: rescaled sums (the (m, l) rows are L2-hot from pass 1).
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        float2 ml[kBatch];
+        float av[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const int s = w + (b * kBatch + i) * kCombineWarps;
+            const bool in = s < c.n_splits;
+            ml[i] = in ? c.part_ml[(size_t)s * c.n_q_heads + hq] : make_float2(-INFINITY, 0.f);
+            av[i] = in ? c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const float f = exp2_approx(ml[i].x - Ms);
+            L = fmaf(ml[i].y, f, L);
+            A = fmaf(av[i], f, A);
+        }
     }
-    if (s < c.n_splits) {
-        const float2 ml0 = c.part_ml[(size_t)s * c.n_q_heads + hq];
-        const float f0 = exp2_approx(ml0.x - Ms);
-        L = fmaf(ml0.y, f0, L);
-        A0 = fmaf(c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d], f0, A0);
-    }
-    if ((threadIdx.x & 31) == 0) s_l[w] = L;
-    s_a[w][threadIdx.x & 31] = A0 + A1;
+    if (lane == 0) s_l[w] = L;
+    s_a[w][lane] = A;
     __syncthreads();
     if (w == 0) {
         float Lt = 0.f, At = 0.f;
 #pragma unroll
         for (int k = 0; k < kCombineWarps; ++k) {
             Lt += s_l[k];
-            At += s_a[k][threadIdx.x];
+            At += s_a[k][lane];
         }
         store_out(c.out, (size_t)hq * kHeadDim + d, At / Lt, c.out_dtype);
     }
-    (void)s_m;
+}
+
+// GKV_NO_PDL=1 turns programmatic dependent launch off (plain stream order).
+bool overlap_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("GKV_NO_PDL");
+        return !(v && v[0] == '1');
+    }();
+    return on;
 }
 
 }  // namespace
@@ -476,6 +510,7 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     const int P = p.pages_per_stage;
     const int n_stages_total = (d.n_pages + P - 1) / P;
     int n_splits = d.n_splits > 0 ? d.n_splits : num_sms;
+    if (n_splits > kMaxSplits) n_splits = kMaxSplits;
     if (n_splits > n_stages_total) n_splits = n_stages_total;
     if (n_splits * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / d.n_q_heads;
     if (n_splits < 1) n_splits = 1;
@@ -483,13 +518,26 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     if (stages_per_split * P > kMaxSplitPages) {  // very long contexts: more splits than SMs
         stages_per_split = kMaxSplitPages / P;
         n_splits = (n_stages_total + stages_per_split - 1) / stages_per_split;
-        if (n_splits * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
+        if (n_splits * d.n_q_heads > kMaxPartialRows || n_splits > kMaxSplits) return cudaErrorInvalidValue;
     }
     p.pages_per_split = stages_per_split * P;
     n_splits = (d.n_pages + p.pages_per_split - 1) / p.pages_per_split;
 
-    paged_decode_kernel<<<n_splits, kThreads, kSmemBytes, stream>>>(k_map, v_map, p);
-    e = cudaGetLastError();
+    // Both launches use programmatic dependent launch: the decode grid's page
+    // stream may start while the previous kernel on the stream finishes (it
+    // waits for that kernel before reading Q / the new K/V row), and the
+    // combine's CTAs are placed while the decode grid runs.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = overlap_enabled() ? 1 : 0;
+    cudaLaunchConfig_t dcfg = {};
+    dcfg.gridDim = dim3(n_splits);
+    dcfg.blockDim = dim3(kThreads);
+    dcfg.dynamicSmemBytes = kSmemBytes;
+    dcfg.stream = stream;
+    dcfg.attrs = attr;
+    dcfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&dcfg, paged_decode_kernel, k_map, v_map, p);
     if (e != cudaSuccess) return e;
 
     CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits};
@@ -498,9 +546,6 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     cfg.blockDim = dim3(kCombineWarps * 32);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel, c);

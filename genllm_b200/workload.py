@@ -112,3 +112,21 @@ class DecodeWorkload:
         out = self.hq_local * self.D * 2
         table = n_pages * 8
         return kv_read + new_kv + q + out + table
+
+
+def allgather_heads(local_out, full_out, group=None):
+    """All-gather each rank's query-head block of a layer output into
+    full_out ([.., Hq, .., D] with the rank-major head order of shard_heads).
+    NCCL: one all_gather_into_tensor; other backends (gloo, for CPU tests):
+    all_gather into a list."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    flat = full_out.view(world, -1)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(flat, local_out.contiguous().view(-1), group=group)
+    else:
+        parts = [torch.empty_like(flat[0]) for _ in range(world)]
+        dist.all_gather(parts, local_out.contiguous().view(-1), group=group)
+        for r in range(world):
+            flat[r].copy_(parts[r])
+    return full_out
