@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor cores")
     ap.add_argument("--no-kernel-events", action="store_true",
                     help="skip the per-launch CUDA events (kernel time then comes from the step time)")
     return ap.parse_args()
@@ -208,6 +210,79 @@ def cpu_step(args):
 
 
 # --------------------------------------------------------------------------
+def run_prefill(args):
+    """Config 4: Qwen3-1.7B layer shape (Hq 16, Hkv 8, D 128), an 8192-token
+    prompt in 512-token chunks; each chunk appended into pages and attended
+    causally over all prior pages by the tensor-core kernel. A step = the
+    whole prompt for one layer (cache reset first). Metric: causal-exact
+    attention TFLOP/s (4 * D * Hq * sum of visible keys)."""
+    import torch
+    from genllm_b200.paged_attention import PagedAttentionManager, paged_attention
+
+    hq, hkv, d, chunk, prompt = 16, 8, 128, 512, 8192
+    torch.cuda.set_device(0)
+    m = PagedAttentionManager(0)
+    m.init_layer(0, hkv, d)
+    m.reserve_layer(0, prompt // 16 + 8)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    n_chunks = prompt // chunk
+    Q = [torch.randn(1, hq, chunk, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(n_chunks)]
+    K = [torch.randn(1, hkv, chunk, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(n_chunks)]
+    V = [torch.randn(1, hkv, chunk, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(n_chunks)]
+    out = torch.empty(1, hq, chunk, d, dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(events=None):
+        m.reset_layer(0)
+        for c in range(n_chunks):
+            if events is not None:
+                events[c][0].record(stream)
+            paged_attention(m, 0, Q[c], K[c], V[c], out=out)
+            if events is not None:
+                events[c][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    flops = 4.0 * d * hq * sum(p + 1 for p in range(prompt))
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_chunks)]
+    step(ev)
+    torch.cuda.synchronize()
+    chunk_ms = [a.elapsed_time(b) for a, b in ev]
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        peak, src = 1590.0, "fallback 1.59 PFLOP/s"
+    tflops = flops / (ms / 1e3) / 1e12
+    last = chunk_ms[-1]
+    last_flops = 4.0 * d * hq * sum(p + 1 for p in range(prompt - chunk, prompt))
+    line = {"metric": "chunked-prefill paged attention TFLOP/s (causal-exact), Qwen3-1.7B layer shape",
+            "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 4: 8192-token prompt in 16 chunks of 512, append + causal attention "
+                                   "over all prior pages", "n_q_heads": hq, "n_kv_heads": hkv, "head_dim": d},
+            "gpu_launches": 2 * n_chunks * args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(last_flops / (last / 1e3) / 1e12, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(last_flops / (last / 1e3) / 1e12 / peak, 4),
+                         "traffic": None, "peak_source": src,
+                         "kernel": "prefill_tc_kernel (+ kv_append_kernel), last chunk (8192 visible keys)",
+                         "chunk_ms": [round(x, 4) for x in chunk_ms]},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -216,6 +291,9 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.workload == "prefill":
+        run_prefill(args)
         return
 
     import torch
