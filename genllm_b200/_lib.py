@@ -74,6 +74,8 @@ SIGNATURES = {
     "gkv_append_kv_raw": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), vp, vp, i32, vp], C.c_int),
     "gkv_paged_attention_raw": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), vp, vp, vp, vp, i32, i32,
                                  C.c_float, i32, i32, vp], C.c_int),
+    "gkv_paged_decode_static_scratch": ([C.POINTER(PoolDesc), vp, i32, vp, vp, vp, vp, i32, C.c_float, i32, vp],
+                                        C.c_int),
 }
 
 

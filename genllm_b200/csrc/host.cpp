@@ -100,6 +100,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 namespace gkv {
 
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 static bool encode(CUtensorMap* m, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
                    const cuuint32_t* box, CUtensorMapSwizzle swz, const char** why) {
     auto enc = tensor_map_encoder();

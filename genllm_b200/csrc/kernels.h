@@ -78,6 +78,9 @@ struct PrefillLaunch {
     int32_t causal;
 };
 
+// Record the message gkv_last_error() returns on this host thread.
+void set_last_error(const char* msg);
+
 // Tensor maps of the tensor-core prefill: the pool's K/V with 128-byte
 // swizzle, box {64, 1, 16}; the chunk's Q [Hq][S][128], box {64, 128, 1}.
 bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map,

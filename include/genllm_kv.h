@@ -229,6 +229,32 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
                             void* out, int32_t n_q_heads, int32_t seq_len, float scale,
                             int32_t causal, int32_t out_dtype, gkv_stream_t stream);
 
+/* ======================= no-allocation decode ============================ */
+
+/* No counterpart in the reference. One fused decode step (append the token
+ * at position n_prior into its page, then attend Q over all n_prior + 1
+ * tokens) for callers that may not allocate device memory — for example code
+ * running under a host framework that owns every device allocation through
+ * its own arena, or a latency-critical loop that cannot afford cudaMalloc's
+ * cost or implicit synchronisation. Nothing is allocated: the split-K scratch
+ * is a fixed 2 MiB + 32 KiB array inside the library that every GPU loading
+ * it keeps until the process exits.
+ *   device_table: [n_pages][2] {k_id, v_id} int32 in device memory, holding
+ *   every page up to and including the one that receives the new token.
+ *   Q [Hq][128], K and V [Hkv][128] (this step's token), out [Hq][128].
+ * Limits: head_dim 128, bf16 pages, 1-8 kv heads, group size 1/2/4/8, split
+ * count x Hq <= 4096 (fewer splits for larger Hq), context <= 1000 pages per
+ * split; larger requests return GKV_ERR_INVALID / GKV_ERR_UNSUPPORTED.
+ * The first call on a device looks up the scratch address on the current
+ * device; make that first call before any stream capture. All calls share
+ * the one scratch array (it keeps the previous call's contents), so calls
+ * that overlap on the GPU — other streams, other threads — race; order them.
+ * The device error word is cleared at the start of each call. */
+int gkv_paged_decode_static_scratch(const gkv_pool_desc* pool, const int32_t* device_table,
+                                    int32_t n_prior, const void* Q, const void* K, const void* V,
+                                    void* out, int32_t n_q_heads, float scale, int32_t out_dtype,
+                                    gkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
