@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--pool", type=int, default=0, help="pages per pool (0: max(4096, ctx/16 + 64))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
@@ -55,10 +56,14 @@ def parse():
     return ap.parse_args()
 
 
+def pool_pages(args):
+    return args.pool or max(POOL, args.ctx // 16 + 64)
+
+
 def config(args, world):
     return {"workload": "Qwen3-4B layer-shape paged-attention decode, 36 layers back to back",
             "n_q_heads": HQ, "n_kv_heads": HKV, "head_dim": D, "layers": args.layers, "ctx": args.ctx,
-            "page_size": 16, "pool_pages": POOL, "block_table": "seeded random permutation (fragmented)",
+            "page_size": 16, "pool_pages": pool_pages(args), "block_table": "seeded random permutation (fragmented)",
             "batch": 1, "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
             "l2": "inputs larger than L2 (36 x 128 MiB of KV per step), no flush"}
 
@@ -304,7 +309,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     from genllm_b200.workload import DecodeWorkload, allgather_heads
 
-    wl = DecodeWorkload(local, n_layers=args.layers, ctx=args.ctx, pool_pages=POOL, n_q_heads=HQ, n_kv_heads=HKV,
+    wl = DecodeWorkload(local, n_layers=args.layers, ctx=args.ctx, pool_pages=pool_pages(args), n_q_heads=HQ, n_kv_heads=HKV,
                         head_dim=D, seed=0, world=world, rank=rank)
     stream = torch.cuda.current_stream()
     sh = __import__("ctypes").c_void_p(stream.cuda_stream)

@@ -10,7 +10,9 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libgenllm_kv.so")
+# GKV_LIB points at another build of the same library (e.g. an instrumented
+# one); by default the in-tree build is used.
+LIB_PATH = os.environ.get("GKV_LIB") or os.path.join(_HERE, "libgenllm_kv.so")
 
 GKV_OK = 0
 GKV_ERR_INVALID = 1

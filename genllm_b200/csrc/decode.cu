@@ -39,7 +39,11 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + producer warp
+#ifdef GKV_PROBE_STAGES
+constexpr int kStages = GKV_PROBE_STAGES;
+#else
 constexpr int kStages = 3;
+#endif
 constexpr uint32_t kTileHalf = kPageSlots * 128;     // 16 slots x 128 B (64 dims): 2 KiB
 constexpr uint32_t kTile = 2 * kTileHalf;            // one (page, head) K or V tile: 4 KiB
 constexpr uint32_t kStageKV = kConsumerWarps * kTile;  // 32 KiB of K (or V) per stage
@@ -175,6 +179,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int pi = 0; pi < np; ++pi) {
                     int2 e = ids[i * P + pi];
                     if (e.x < 0) e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
+#ifdef GKV_PROBE_BIGBOX
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const uint32_t t = (uint32_t)(pi * 2 + hf) * Hkv * kTileHalf;
+                        tma_load_3d(sk + t, &k_map, &full[st], hf * 64, e.x * kPageSlots, 0, pol);
+                        tma_load_3d(sv + t, &v_map, &full[st], hf * 64, e.y * kPageSlots, 0, pol);
+                    }
+#else
                     for (int h = 0; h < Hkv; ++h) {
                         const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
                         for (int hf = 0; hf < 2; ++hf) {
@@ -182,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tma_load_3d(sv + t + hf * kTileHalf, &v_map, &full[st], hf * 64, h, e.y * kPageSlots, pol);
                         }
                     }
+#endif
                 }
             }
         }
@@ -226,7 +238,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int lp = p0 + i * P + pslot;
             const bool have = active && lp < p1 && ok_wait;
             const int2 e = have ? ids[lp - p0] : make_int2(-1, -1);
+#ifdef GKV_PROBE_SKIP_COMPUTE
+            const bool use = false;  // measurement build: page stream only
+            (void)e;
+#else
             const bool use = have && e.x >= 0;
+#endif
             if (use) {
                 uint8_t* kt = smem + st * kStageBytes + (uint32_t)(pslot * Hkv + head) * kTile;
                 uint8_t* vt = kt + kStageKV;
@@ -400,6 +417,9 @@ constexpr int kCombineDims = 32;  // dims per CTA (one per lane)
 // merge through shared memory.
 __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_kernel(const CombineParams c) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
+    // Only now may the next launch start: a decode step of the same layer
+    // reads pages and table entries this step's decode grid wrote, and its
+    // page stream begins before it waits for this grid.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int hq = blockIdx.x;
     const int lane = threadIdx.x & 31;
@@ -407,26 +427,8 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     const int w = threadIdx.x >> 5;
     constexpr int kBatch = 10;  // splits per warp in flight at once; 2 batches (n_splits <= 160)
     __shared__ float s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims], s_m[kCombineWarps];
-    // Pass 1: the global max over split maxima (loads issued together).
-    float M = -INFINITY;
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-        float mx[kBatch];
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-            const int s = w + (b * kBatch + i) * kCombineWarps;
-            mx[i] = s < c.n_splits ? c.part_ml[(size_t)s * c.n_q_heads + hq].x : -INFINITY;
-        }
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) M = fmaxf(M, mx[i]);
-    }
-    if (lane == 0) s_m[w] = M;
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kCombineWarps; ++k) M = fmaxf(M, s_m[k]);
-    const float Ms = M == -INFINITY ? 0.f : M;
-    // Pass 2: rescaled sums (the (m, l) rows are L2-hot from pass 1).
-    float L = 0.f, A = 0.f;
+    // One pass with an online rescale: each batch's loads are issued together.
+    float M = -INFINITY, L = 0.f, A = 0.f;
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
         float2 ml[kBatch];
@@ -438,22 +440,38 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
             ml[i] = in ? c.part_ml[(size_t)s * c.n_q_heads + hq] : make_float2(-INFINITY, 0.f);
             av[i] = in ? c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d] : 0.f;
         }
+        float mb = M;
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) mb = fmaxf(mb, ml[i].x);
+        const float ms = mb == -INFINITY ? 0.f : mb;
+        const float r = exp2_approx(M - ms);
+        L *= r;
+        A *= r;
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const float f = exp2_approx(ml[i].x - Ms);
+            const float f = exp2_approx(ml[i].x - ms);
             L = fmaf(ml[i].y, f, L);
             A = fmaf(av[i], f, A);
         }
+        M = mb;
     }
-    if (lane == 0) s_l[w] = L;
+    if (lane == 0) {
+        s_m[w] = M;
+        s_l[w] = L;
+    }
     s_a[w][lane] = A;
     __syncthreads();
     if (w == 0) {
+        float Mt = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kCombineWarps; ++k) Mt = fmaxf(Mt, s_m[k]);
+        const float ms = Mt == -INFINITY ? 0.f : Mt;
         float Lt = 0.f, At = 0.f;
 #pragma unroll
         for (int k = 0; k < kCombineWarps; ++k) {
-            Lt += s_l[k];
-            At += s_a[k][lane];
+            const float f = exp2_approx(s_m[k] - ms);
+            Lt = fmaf(s_l[k], f, Lt);
+            At = fmaf(s_a[k][lane], f, At);
         }
         store_out(c.out, (size_t)hq * kHeadDim + d, At / Lt, c.out_dtype);
     }
