@@ -116,6 +116,14 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+#ifdef GKV_PROBE_TIMELINE
+__device__ unsigned long long g_probe_tl[4096 * 8];
+#define PROBE_T(k) \
+    if (threadIdx.x == 0) g_probe_tl[blockIdx.x * 8 + (k)] = global_timer_ns();
+#else
+#define PROBE_T(k)
+#endif
+
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
                         const DecodeParams a) {
@@ -124,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint64_t* empty = full + kStages;
 
+    PROBE_T(0);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int split = blockIdx.x;
@@ -142,59 +151,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     // be scheduled now (it waits for this grid's completion itself).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // This split's page ids, bounds-checked once, into shared memory (a bad id
-    // becomes {-1, -1}: loaded as page 0, skipped by the consumer).
-    int2* ids = reinterpret_cast<int2*>(smem + kOffIds);
-    for (int i = threadIdx.x; i < p1 - p0; i += kThreads) {
+    // Stage i of this split: its np pages, every kv head, both 64-dim halves of
+    // K and V, one TMA box {64, 1, 16} each, completing on full[i % kStages].
+    const uint64_t pol = l2_policy_evict_first();
+    auto issue_stage = [&](int i, auto&& entry_of) {
+        const int st = i % kStages;
+        uint8_t* sk = smem + st * kStageBytes;
+        uint8_t* sv = sk + kStageKV;
+        const int np = min(P, p1 - (p0 + i * P));
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[st], (uint32_t)(np * Hkv) * 2u * kTile);
+        for (int pi = 0; pi < np; ++pi) {
+            int2 e = entry_of(i * P + pi);
+            if (e.x < 0) e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
+            for (int h = 0; h < Hkv; ++h) {
+                const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
+                for (int hf = 0; hf < 2; ++hf) {
+                    tma_load_3d(sk + t + hf * kTileHalf, &k_map, &full[st], hf * 64, h, e.x * kPageSlots, pol);
+                    tma_load_3d(sv + t + hf * kTileHalf, &v_map, &full[st], hf * 64, h, e.y * kPageSlots, pol);
+                }
+            }
+        }
+    };
+    // A page id, bounds-checked: a bad id becomes {-1, -1} (loaded as page 0,
+    // skipped by the consumer) and sets the error bit.
+    auto checked = [&](int i) {
         int2 e = page_entry(a, p0 + i);
         if (!entry_ok(a, e)) {
             atomicOr(a.err, kErrBadPage);
             e = make_int2(-1, -1);
         }
-        ids[i] = e;
-    }
-    if (threadIdx.x == 0) {
+        return e;
+    };
+
+    const int pre = n_stages < kStages ? n_stages : kStages;
+    int2* ids = reinterpret_cast<int2*>(smem + kOffIds);
+    if (threadIdx.x == kConsumerWarps * 32) {
+        // Producer: barriers, then the first stages straight from the table,
+        // while the other threads cache the split's remaining ids.
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
         fence_mbar_init();
+        for (int i = 0; i < pre; ++i) issue_stage(i, checked);
+    } else {
+        for (int i = pre * P + (int)threadIdx.x; i < p1 - p0; i += kConsumerWarps * 32) ids[i] = checked(i);
     }
     __syncthreads();
+    PROBE_T(1);
 
     if (warp == kConsumerWarps) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
-            for (int i = 0; i < n_stages; ++i) {
+            for (int i = kStages; i < n_stages; ++i) {
                 const int st = i % kStages;
-                if (i >= kStages && !mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1)) {
-                    atomicOr(a.err, kErrTimeout);
-                }
-                uint8_t* sk = smem + st * kStageBytes;
-                uint8_t* sv = sk + kStageKV;
-                const int np = min(P, p1 - (p0 + i * P));
-                fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&full[st], (uint32_t)(np * Hkv) * 2u * kTile);
-                for (int pi = 0; pi < np; ++pi) {
-                    int2 e = ids[i * P + pi];
-                    if (e.x < 0) e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
-#ifdef GKV_PROBE_BIGBOX
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const uint32_t t = (uint32_t)(pi * 2 + hf) * Hkv * kTileHalf;
-                        tma_load_3d(sk + t, &k_map, &full[st], hf * 64, e.x * kPageSlots, 0, pol);
-                        tma_load_3d(sv + t, &v_map, &full[st], hf * 64, e.y * kPageSlots, 0, pol);
-                    }
-#else
-                    for (int h = 0; h < Hkv; ++h) {
-                        const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
-                        for (int hf = 0; hf < 2; ++hf) {
-                            tma_load_3d(sk + t + hf * kTileHalf, &k_map, &full[st], hf * 64, h, e.x * kPageSlots, pol);
-                            tma_load_3d(sv + t + hf * kTileHalf, &v_map, &full[st], hf * 64, h, e.y * kPageSlots, pol);
-                        }
-                    }
-#endif
-                }
+                if (!mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1)) atomicOr(a.err, kErrTimeout);
+                issue_stage(i, [&](int k) { return ids[k]; });
             }
         }
     } else {
@@ -234,10 +247,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < n_stages; ++i) {
             const int st = i % kStages;
             const bool ok_wait = mbar_wait_bounded(&full[st], (i / kStages) & 1);
+            if (i == 0) { PROBE_T(2); }
             if (!ok_wait && lane == 0) atomicOr(a.err, kErrTimeout);
             const int lp = p0 + i * P + pslot;
             const bool have = active && lp < p1 && ok_wait;
-            const int2 e = have ? ids[lp - p0] : make_int2(-1, -1);
+            const int2 e = !have ? make_int2(-1, -1) : (i < pre ? checked(lp - p0) : ids[lp - p0]);
 #ifdef GKV_PROBE_SKIP_COMPUTE
             const bool use = false;  // measurement build: page stream only
             (void)e;
@@ -351,6 +365,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
+        if (P == 1) {
+            // One warp per kv head: its state is already this split's partial
+            // for the head's G query heads; write it straight out.
+            const int Hq = Hkv * G;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int n = 2 * t + half;
+                if (active && n < G) {
+                    const size_t row = (size_t)split * Hq + head * G + n;
+                    float* dst = a.part_acc + row * kHeadDim;
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        dst[mt * 16 + g] = acc[mt][half];
+                        dst[mt * 16 + g + 8] = acc[mt][2 + half];
+                    }
+                    if (g == 0) a.part_ml[row] = half ? make_float2(m1, l1) : make_float2(m0, l0);
+                }
+            }
+        } else {
         // Per-warp state to shared memory (stage buffers are free: the producer
         // issued nothing beyond n_stages and every stage was consumed).
         __syncwarp();
@@ -371,11 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             w_ml[(warp * 8 + 2 * t + 1) * 2 + 0] = active ? m1 : -INFINITY;
             w_ml[(warp * 8 + 2 * t + 1) * 2 + 1] = active ? l1 : 0.f;
         }
+        }
     }
     __syncthreads();
+    PROBE_T(3);
 
     // ---- merge warps of the same head; write this split's partials ---------
-    {
+    if (P > 1) {
         float* w_acc = reinterpret_cast<float*>(smem);
         float* w_ml = w_acc + kConsumerWarps * 8 * kHeadDim;
         const int Hq = Hkv * G;
@@ -397,6 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (d == 0) a.part_ml[row] = make_float2(M, L);
         }
     }
+#ifdef GKV_PROBE_TIMELINE
+    __syncthreads();
+    PROBE_T(4);
+#endif
 }
 
 struct CombineParams {
@@ -570,3 +609,9 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
 }
 
 }  // namespace gkv
+
+#ifdef GKV_PROBE_TIMELINE
+extern "C" int gkv_probe_read_timeline(unsigned long long* out, int n) {
+    return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_tl, sizeof(unsigned long long) * n);
+}
+#endif

@@ -120,12 +120,6 @@ static bool encode(CUtensorMap* m, void* base, int rank, const cuuint64_t* dims,
     return true;
 }
 
-#ifdef GKV_PROBE_BIGBOX
-bool encode_probe(CUtensorMap* m, void* base, const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
-                  const char** why) {
-    return encode(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
-}
-#endif
 
 bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
     cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)pool.n_kv_heads, (cuuint64_t)pool.pool_pages * 16};
@@ -403,21 +397,7 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
         d.n_pages = n_pages;
         d.scale = scale;
         d.n_splits = 0;
-#ifdef GKV_PROBE_BIGBOX
-        CUtensorMap bk, bv;
-        {
-            const char* why = nullptr;
-            cuuint64_t dims[3] = {128, (cuuint64_t)pool->pool_pages * 16, (cuuint64_t)pool->n_kv_heads};
-            cuuint64_t strides[2] = {(cuuint64_t)pool->n_kv_heads * 256, 256};
-            cuuint32_t box[3] = {64, 16, (cuuint32_t)pool->n_kv_heads};
-            if (!gkv::encode_probe(&bk, pool->k_base, dims, strides, box, &why) ||
-                !gkv::encode_probe(&bv, pool->v_base, dims, strides, box, &why))
-                return fail(GKV_ERR_CUDA, "probe map: %s", why);
-        }
-        cudaError_t e = gkv::launch_decode(pv, bk, bv, t->d_table, p, t->scratch, d, t->num_sms, s);
-#else
         cudaError_t e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s);
-#endif
         if (e != cudaSuccess) return cuda_fail(e, "decode launch");
         return GKV_OK;
     }
