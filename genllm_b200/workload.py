@@ -51,6 +51,12 @@ class DecodeWorkload:
         self.scale = 1.0 / float(head_dim) ** 0.5
         self.mgr = PagedAttentionManager(device)
         self.layers = []
+        # All layers' step inputs (Q | K | V) in one buffer and all outputs in
+        # another, so a host round trip is one copy each way.
+        hq_l, hkv_l = qe - qb, ke - kb
+        self.in_width = (hq_l + 2 * hkv_l) * head_dim
+        self.inbuf = torch.empty((n_layers, self.in_width), dtype=torch.bfloat16, device=self.device)
+        self.outbuf = torch.empty((n_layers, hq_l * head_dim), dtype=torch.bfloat16, device=self.device)
         n_pages = (ctx + PAGE - 1) // PAGE
         for l in range(n_layers):
             rng = np.random.default_rng(seed * 1000 + l)
@@ -80,8 +86,15 @@ class DecodeWorkload:
             q = torch.randn((1, n_q_heads, 1, head_dim), generator=g, device=self.device)[:, qb:qe].to(torch.bfloat16)
             k = torch.randn((1, n_kv_heads, 1, head_dim), generator=g, device=self.device)[:, kb:ke].to(torch.bfloat16)
             v = torch.randn((1, n_kv_heads, 1, head_dim), generator=g, device=self.device)[:, kb:ke].to(torch.bfloat16)
-            out_t = torch.empty((1, self.hq_local, 1, head_dim), dtype=torch.bfloat16, device=self.device)
-            self.layers.append(LayerBufs(q.contiguous(), k.contiguous(), v.contiguous(), out_t))
+            row = self.inbuf[l]
+            qv = row[: hq_l * head_dim].view(1, hq_l, 1, head_dim)
+            kv = row[hq_l * head_dim: (hq_l + hkv_l) * head_dim].view(1, hkv_l, 1, head_dim)
+            vv = row[(hq_l + hkv_l) * head_dim:].view(1, hkv_l, 1, head_dim)
+            qv.copy_(q)
+            kv.copy_(k)
+            vv.copy_(v)
+            out_t = self.outbuf[l].view(1, hq_l, 1, head_dim)
+            self.layers.append(LayerBufs(qv, kv, vv, out_t))
         torch.cuda.synchronize(self.device)
         self._fn = _lib.lib().gkv_paged_attention
         self._args = [
