@@ -184,19 +184,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         return e;
     };
 
-    const int pre = n_stages < kStages ? n_stages : kStages;
     int2* ids = reinterpret_cast<int2*>(smem + kOffIds);
-    if (threadIdx.x == kConsumerWarps * 32) {
-        // Producer: barriers, then the first stages straight from the table,
-        // while the other threads cache the split's remaining ids.
+    for (int i = threadIdx.x; i < p1 - p0; i += kThreads) ids[i] = checked(i);
+    if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
         fence_mbar_init();
-        for (int i = 0; i < pre; ++i) issue_stage(i, checked);
-    } else {
-        for (int i = pre * P + (int)threadIdx.x; i < p1 - p0; i += kConsumerWarps * 32) ids[i] = checked(i);
     }
     __syncthreads();
     PROBE_T(1);
@@ -204,9 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kConsumerWarps) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            for (int i = kStages; i < n_stages; ++i) {
+            for (int i = 0; i < n_stages; ++i) {
                 const int st = i % kStages;
-                if (!mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1)) atomicOr(a.err, kErrTimeout);
+                if (i >= kStages && !mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1))
+                    atomicOr(a.err, kErrTimeout);
                 issue_stage(i, [&](int k) { return ids[k]; });
             }
         }
@@ -251,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok_wait && lane == 0) atomicOr(a.err, kErrTimeout);
             const int lp = p0 + i * P + pslot;
             const bool have = active && lp < p1 && ok_wait;
-            const int2 e = !have ? make_int2(-1, -1) : (i < pre ? checked(lp - p0) : ids[lp - p0]);
+            const int2 e = have ? ids[lp - p0] : make_int2(-1, -1);
 #ifdef GKV_PROBE_SKIP_COMPUTE
             const bool use = false;  // measurement build: page stream only
             (void)e;
@@ -365,15 +361,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
-        if (P == 1) {
-            // One warp per kv head: its state is already this split's partial
-            // for the head's G query heads; write it straight out.
+        // Each warp's state is a partial of its own: split index (CTA, page
+        // slot). The combine kernel merges all of them.
+        if (active) {
             const int Hq = Hkv * G;
+            const int sp = split * P + pslot;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const int n = 2 * t + half;
-                if (active && n < G) {
-                    const size_t row = (size_t)split * Hq + head * G + n;
+                if (n < G) {
+                    const size_t row = (size_t)sp * Hq + head * G + n;
                     float* dst = a.part_acc + row * kHeadDim;
 #pragma unroll
                     for (int mt = 0; mt < 8; ++mt) {
@@ -383,55 +380,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (g == 0) a.part_ml[row] = half ? make_float2(m1, l1) : make_float2(m0, l0);
                 }
             }
-        } else {
-        // Per-warp state to shared memory (stage buffers are free: the producer
-        // issued nothing beyond n_stages and every stage was consumed).
-        __syncwarp();
-        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
-        float* w_acc = reinterpret_cast<float*>(smem);  // [warp][8 heads][128]
-        float* w_ml = w_acc + kConsumerWarps * 8 * kHeadDim;  // [warp][8 heads][2]
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-            const int d = mt * 16 + g;
-            w_acc[(warp * 8 + 2 * t) * kHeadDim + d] = acc[mt][0];
-            w_acc[(warp * 8 + 2 * t + 1) * kHeadDim + d] = acc[mt][1];
-            w_acc[(warp * 8 + 2 * t) * kHeadDim + d + 8] = acc[mt][2];
-            w_acc[(warp * 8 + 2 * t + 1) * kHeadDim + d + 8] = acc[mt][3];
-        }
-        if (g == 0) {
-            w_ml[(warp * 8 + 2 * t) * 2 + 0] = active ? m0 : -INFINITY;
-            w_ml[(warp * 8 + 2 * t) * 2 + 1] = active ? l0 : 0.f;
-            w_ml[(warp * 8 + 2 * t + 1) * 2 + 0] = active ? m1 : -INFINITY;
-            w_ml[(warp * 8 + 2 * t + 1) * 2 + 1] = active ? l1 : 0.f;
-        }
         }
     }
     __syncthreads();
     PROBE_T(3);
 
-    // ---- merge warps of the same head; write this split's partials ---------
-    if (P > 1) {
-        float* w_acc = reinterpret_cast<float*>(smem);
-        float* w_ml = w_acc + kConsumerWarps * 8 * kHeadDim;
-        const int Hq = Hkv * G;
-        const int n_warps_used = min(kConsumerWarps, P * Hkv);
-        for (int idx = threadIdx.x; idx < Hq * kHeadDim; idx += kThreads) {
-            const int hq = idx / kHeadDim, d = idx % kHeadDim;
-            const int h = hq / G, gg = hq % G;
-            float M = -INFINITY;
-            for (int w = h; w < n_warps_used; w += Hkv) M = fmaxf(M, w_ml[(w * 8 + gg) * 2]);
-            const float Ms = M == -INFINITY ? 0.f : M;
-            float L = 0.f, A = 0.f;
-            for (int w = h; w < n_warps_used; w += Hkv) {
-                const float f = exp2_approx(w_ml[(w * 8 + gg) * 2] - Ms);
-                L = fmaf(w_ml[(w * 8 + gg) * 2 + 1], f, L);
-                A = fmaf(w_acc[(w * 8 + gg) * kHeadDim + d], f, A);
-            }
-            const size_t row = (size_t)split * Hq + hq;
-            a.part_acc[row * kHeadDim + d] = A;
-            if (d == 0) a.part_ml[row] = make_float2(M, L);
-        }
-    }
 #ifdef GKV_PROBE_TIMELINE
     __syncthreads();
     PROBE_T(4);
@@ -448,7 +401,6 @@ struct CombineParams {
 };
 
 constexpr int kCombineWarps = 8;
-constexpr int kMaxSplits = 160;  // = kCombineWarps * splits held per warp in the combine
 constexpr int kCombineDims = 32;  // dims per CTA (one per lane)
 
 // Grid (Hq, 128 / 32): warp w of a CTA folds splits w, w + 8, ... for the
@@ -464,12 +416,11 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     const int lane = threadIdx.x & 31;
     const int d = blockIdx.y * kCombineDims + lane;
     const int w = threadIdx.x >> 5;
-    constexpr int kBatch = 10;  // splits per warp in flight at once; 2 batches (n_splits <= 160)
+    constexpr int kBatch = 19;  // splits per warp in flight at once (147 splits: one round)
     __shared__ float s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims], s_m[kCombineWarps];
     // One pass with an online rescale: each batch's loads are issued together.
     float M = -INFINITY, L = 0.f, A = 0.f;
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b * kBatch * kCombineWarps < c.n_splits; ++b) {
         float2 ml[kBatch];
         float av[kBatch];
 #pragma unroll
@@ -567,15 +518,14 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     const int P = p.pages_per_stage;
     const int n_stages_total = (d.n_pages + P - 1) / P;
     int n_splits = d.n_splits > 0 ? d.n_splits : num_sms;
-    if (n_splits > kMaxSplits) n_splits = kMaxSplits;
     if (n_splits > n_stages_total) n_splits = n_stages_total;
-    if (n_splits * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / d.n_q_heads;
+    if (n_splits * P * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / (P * d.n_q_heads);
     if (n_splits < 1) n_splits = 1;
     int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
     if (stages_per_split * P > kMaxSplitPages) {  // very long contexts: more splits than SMs
         stages_per_split = kMaxSplitPages / P;
         n_splits = (n_stages_total + stages_per_split - 1) / stages_per_split;
-        if (n_splits * d.n_q_heads > kMaxPartialRows || n_splits > kMaxSplits) return cudaErrorInvalidValue;
+        if (n_splits * P * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
     }
     p.pages_per_split = stages_per_split * P;
     n_splits = (d.n_pages + p.pages_per_split - 1) / p.pages_per_split;
@@ -597,7 +547,7 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     e = cudaLaunchKernelEx(&dcfg, paged_decode_kernel, k_map, v_map, p);
     if (e != cudaSuccess) return e;
 
-    CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits};
+    CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits * P};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d.n_q_heads, kHeadDim / kCombineDims);
     cfg.blockDim = dim3(kCombineWarps * 32);

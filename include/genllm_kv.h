@@ -242,9 +242,9 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
  *   device_table: [n_pages][2] {k_id, v_id} int32 in device memory, holding
  *   every page up to and including the one that receives the new token.
  *   Q [Hq][128], K and V [Hkv][128] (this step's token), out [Hq][128].
- * Limits: head_dim 128, bf16 pages, 1-8 kv heads, group size 1/2/4/8, split
- * count x Hq <= 4096 (fewer splits for larger Hq), context <= 1000 pages per
- * split; larger requests return GKV_ERR_INVALID / GKV_ERR_UNSUPPORTED.
+ * Limits: head_dim 128, bf16 pages, 1-8 kv heads, group size 1/2/4/8; the
+ * fixed scratch holds 4096 partial rows (splits x (8 / Hkv) x Hq), so larger
+ * Hq gets fewer splits; context <= 1000 pages per split; larger requests return GKV_ERR_INVALID / GKV_ERR_UNSUPPORTED.
  * The first call on a device looks up the scratch address on the current
  * device; make that first call before any stream capture. All calls share
  * the one scratch array (it keeps the previous call's contents), so calls
