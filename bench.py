@@ -120,6 +120,21 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
+def profiled_traffic(args, world):
+    """DRAM bytes (read + write) of one paged_decode_kernel launch from the
+    committed ncu summary of this exact configuration, or None."""
+    if world != 1 or args.ctx != CTX:
+        return None
+    try:
+        with open(os.path.join(ROOT, "profiles", "paged_decode_kernel_qwen3_4b_32k.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def measured_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -442,7 +457,10 @@ def main():
         "gpu_launches": 2 * args.steps * args.layers,
         "host_enqueue_ms_per_step": round(1e3 * host_enqueue_s / args.steps, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args, world),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of paged_decode_kernel "
+                                       "(profiles/paged_decode_kernel_qwen3_4b_32k.md)",
+                     "peak_source": peak_src,
                      "kernel": "paged_decode_kernel + paged_decode_combine_kernel (one decode step of one layer)",
                      "kernel_avg_us": round(1e3 * kern_max, 3),
                      "bytes_per_launch": round(per_launch_bytes)},
