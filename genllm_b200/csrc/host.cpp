@@ -420,7 +420,7 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
         CUtensorMap q_map;
         const char* why = nullptr;
         if (!gkv::encode_q_map_sw128(pl.q, n_q_heads, seq_len, &q_map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
-        e = gkv::launch_prefill_tc(pv, q_map, t->k_map_sw, t->v_map_sw, t->d_table, pl, t->scratch.err, s);
+        e = gkv::launch_prefill_tc(pv, q_map, t->k_map_sw, t->v_map_sw, t->d_table, pl, t->scratch.err, t->num_sms, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
     return GKV_OK;

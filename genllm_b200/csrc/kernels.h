@@ -93,7 +93,7 @@ bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, C
 cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map,
                               const CUtensorMap& k_map, const CUtensorMap& v_map,
                               const int2* table, const PrefillLaunch& p, uint32_t* err,
-                              cudaStream_t stream);
+                              int num_sms, cudaStream_t stream);
 
 // The same on CUDA cores (one warp per query row); kept as an independent
 // second implementation for cross-checking.

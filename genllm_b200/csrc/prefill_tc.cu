@@ -84,7 +84,12 @@ __global__ void __launch_bounds__(128, 1)
     const int first_q_abs = a.total - S + q0;
     const int last_q_abs = min(a.total - 1, first_q_abs + kBM - 1);
     const int kv_end = a.causal ? last_q_abs + 1 : a.total;
-    const int n_tiles = (kv_end + kBN - 1) / kBN;
+    const int n_tiles_all = (kv_end + kBN - 1) / kBN;
+    // KV split across the CTAs of a cluster (grid z = cluster size): this CTA
+    // takes tiles [j0, j0 + n_tiles) and the leader merges the results.
+    const int rank = blockIdx.z, n_split = gridDim.z;
+    const int j0 = rank * n_tiles_all / n_split;
+    const int n_tiles = (rank + 1) * n_tiles_all / n_split - j0;
 
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
@@ -118,7 +123,7 @@ __global__ void __launch_bounds__(128, 1)
         uint64_t* bar = &bar_kv[st];
         mbar_arrive_expect_tx(bar, 2 * kTile);
         for (int i = 0; i < kPagesPerTile; ++i) {
-            int lp = j * kPagesPerTile + i;
+            int lp = (j0 + j) * kPagesPerTile + i;
             if (lp >= a.n_pages) lp = a.n_pages - 1;  // beyond the cache: rows are masked / zeroed
             int2 e = a.table[lp];
             if (e.x < 0 || e.x >= a.pool_pages || e.y < 0 || e.y >= a.pool_pages) {
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(128, 1)
         mbar_arrive_expect_tx(bar_q, kTile);
         tma_load_3d(smem + kOffQ, &q_map, bar_q, 0, q0, hq, pol);
         tma_load_3d(smem + kOffQ + kHalf, &q_map, bar_q, 64, q0, hq, pol);
-        issue_kv(0);
+        if (n_tiles > 0) issue_kv(0);
         if (n_tiles > 1) issue_kv(1);
     }
 
@@ -160,7 +165,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
         wait(&bar_kv[st], (j >> 1) & 1);
-        const int key0 = j * kBN;
+        const int key0 = (j0 + j) * kBN;
         // Zero V rows past the cache in this tile.
         const int valid_rows = min(kBN, a.total - key0);
         if (r >= valid_rows) {
@@ -271,26 +276,78 @@ __global__ void __launch_bounds__(128, 1)
         }
     }
 
-    wait(bar_o, (n_tiles - 1) & 1);
+    if (n_tiles > 0) wait(bar_o, (n_tiles - 1) & 1);
+    if (tid == 0 && n_tiles == 0) wait(bar_q, 0);  // the Q load must land before the CTA exits
     tc::fence_after_sync();
-    const float inv = 1.f / l_run;
-    const int q = q0 + r;
+    float o[128];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        float o[32];
-        tc::ld32(t_o + c * 32, o);  // warp-collective: executed even on the error path
-        tc::wait_ld();
-        if (ok && q < S) {
-            const size_t base = ((size_t)hq * S + q) * kHeadDim + c * 32;
-            if (a.out_dtype == 0) {
-                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
+    for (int c = 0; c < 4; ++c) tc::ld32(t_o + c * 32, *reinterpret_cast<float(*)[32]>(&o[c * 32]));
+    tc::wait_ld();  // warp-collective: executed even on the error path
+    if (n_tiles == 0) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-            } else {
+        for (int i = 0; i < 128; ++i) o[i] = 0.f;
+    }
+    float m_fin = m_run, l_fin = l_run;
+    if (n_split > 1) {
+        // Merge through distributed shared memory: the other CTAs of the
+        // cluster send (m, l, O row) into the leader's (now idle) buffers.
+        tc::fence_before_sync();
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        constexpr uint32_t kRecvO = 128 * kHeadDim * 4;  // 64 KiB per sending CTA
+        constexpr uint32_t kRecvMl = 3 * kRecvO;
+        if (rank > 0) {
+            const uint32_t local = smem_addr(smem + (rank - 1) * kRecvO + r * kHeadDim * 4);
+            uint32_t remote;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(local));
 #pragma unroll
-                for (int i = 0; i < 32; ++i) store_out(a.out, base + i, o[i] * inv, a.out_dtype);
+            for (int i = 0; i < 32; ++i)
+                asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote + i * 16), "f"(o[4 * i]),
+                             "f"(o[4 * i + 1]), "f"(o[4 * i + 2]), "f"(o[4 * i + 3])
+                             : "memory");
+            const uint32_t lml = smem_addr(smem + kRecvMl + ((rank - 1) * 128 + r) * 8);
+            uint32_t rml;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rml) : "r"(lml));
+            asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(rml), "f"(m_run), "f"(l_run) : "memory");
+        }
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        if (rank == 0) {
+            float M = m_run;
+            for (int k = 1; k < n_split; ++k) M = fmaxf(M, reinterpret_cast<const float2*>(smem + kRecvMl)[(k - 1) * 128 + r].x);
+            const float Ms = M == -INFINITY ? 0.f : M;
+            const float f0 = exp2_approx(m_run - Ms);
+            l_fin = l_run * f0;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) o[i] *= f0;
+            for (int k = 1; k < n_split; ++k) {
+                const float2 ml = reinterpret_cast<const float2*>(smem + kRecvMl)[(k - 1) * 128 + r];
+                const float f = exp2_approx(ml.x - Ms);
+                l_fin = fmaf(ml.y, f, l_fin);
+                const float4* src = reinterpret_cast<const float4*>(smem + (k - 1) * kRecvO + r * kHeadDim * 4);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float4 v = src[i];
+                    o[4 * i] = fmaf(v.x, f, o[4 * i]);
+                    o[4 * i + 1] = fmaf(v.y, f, o[4 * i + 1]);
+                    o[4 * i + 2] = fmaf(v.z, f, o[4 * i + 2]);
+                    o[4 * i + 3] = fmaf(v.w, f, o[4 * i + 3]);
+                }
             }
+            m_fin = M;
+        }
+    }
+    (void)m_fin;
+    const float inv = 1.f / l_fin;
+    const int q = q0 + r;
+    if (rank == 0 && ok && q < S) {
+        const size_t base = ((size_t)hq * S + q) * kHeadDim;
+        if (a.out_dtype == 0) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 128; ++i) store_out(a.out, base + i, o[i] * inv, a.out_dtype);
         }
     }
     if (!ok) atomicOr(a.err, kErrTimeout);
@@ -306,7 +363,7 @@ __global__ void __launch_bounds__(128, 1)
 
 cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const CUtensorMap& k_map,
                               const CUtensorMap& v_map, const int2* table, const PrefillLaunch& p, uint32_t* err,
-                              cudaStream_t stream) {
+                              int num_sms, cudaStream_t stream) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -329,9 +386,25 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
     a.pool_pages = pool.pool_pages;
     a.causal = p.causal;
     a.qscale = p.scale * 1.4426950408889634f;
-    dim3 grid((p.seq_len + kBM - 1) / kBM, p.n_q_heads);
-    prefill_tc_kernel<<<grid, 128, kSmemBytes, stream>>>(q_map, k_map, v_map, a);
-    return cudaGetLastError();
+    // Split the KV range over a cluster of up to 3 CTAs while the query tiles
+    // alone would leave SMs idle.
+    const int tiles = ((p.seq_len + kBM - 1) / kBM) * p.n_q_heads;
+    int n_split = num_sms / (tiles > 0 ? tiles : 1);
+    if (n_split > 3) n_split = 3;
+    if (n_split < 1) n_split = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.seq_len + kBM - 1) / kBM, p.n_q_heads, n_split);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = n_split;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, k_map, v_map, a);
 }
 
 }  // namespace gkv
