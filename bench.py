@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor cores")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1: head all-gather fused into the decode (NVLink peer stores) or NCCL all_gather")
     ap.add_argument("--no-kernel-events", action="store_true",
                     help="skip the per-launch CUDA events (kernel time then comes from the step time)")
     return ap.parse_args()
@@ -331,15 +333,35 @@ def main():
     gathered_all = torch.empty((args.layers, HQ * D), dtype=torch.bfloat16, device="cuda")
     gathered = [gathered_all[l].view(1, HQ, 1, D) for l in range(args.layers)]
 
+    hg = None
+    if world > 1 and args.gather == "p2p":
+        import ctypes as C
+        from genllm_b200 import _lib
+        from genllm_b200.gather import HeadGather
+        hg = HeadGather(local, args.layers, HQ)
+        gfn = _lib.lib().gkv_paged_attention_gather
+        gargs = [(wl.mgr.handle, l, C.c_void_p(b.q.data_ptr()), C.c_void_p(b.k.data_ptr()), C.c_void_p(b.v.data_ptr()),
+                  hg.handle, l * hg.layer_bytes, wl.hq_local, C.c_float(wl.scale), _lib.GKV_BF16, sh)
+                 for l, b in enumerate(wl.layers)]
+        gathered_all = hg.full.view(args.layers, HQ * D)
+
+    def layer_call(l):
+        if hg is not None:
+            st = gfn(*gargs[l])
+            if st:
+                _lib.check(st)
+        else:
+            wl.layer_step(l, sh)
+            if world > 1:
+                allgather_heads(wl.layers[l].out, gathered[l])
+
     def step(events=None):
         for l in range(args.layers):
             if events is not None:
                 events[l][0].record(stream)
-            wl.layer_step(l, sh)
+            layer_call(l)
             if events is not None:
                 events[l][1].record(stream)
-            if world > 1:
-                allgather_heads(wl.layers[l].out, gathered[l])
 
     for _ in range(args.warmup):
         step()
@@ -409,9 +431,12 @@ def main():
         wl.inbuf.copy_(h_in, non_blocking=True)
         for l in range(args.layers):
             L = wl.layers[l]
-            paged_attention(wl.mgr, l, L.q, L.k, L.v, out=L.out, scale=wl.scale)
-            if world > 1:
-                allgather_heads(L.out, gathered[l])
+            if hg is not None:
+                hg.decode(wl.mgr, l, L.q, L.k, L.v, wl.scale)
+            else:
+                paged_attention(wl.mgr, l, L.q, L.k, L.v, out=L.out, scale=wl.scale)
+                if world > 1:
+                    allgather_heads(L.out, gathered[l])
         h_out.copy_(gathered_all if world > 1 else wl.outbuf, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         return float(h_out[-1, 0])  # the step's result, read on the host
@@ -455,6 +480,7 @@ def main():
                 "steps": e2e_steps, "ms_per_step": round(te.item() / e2e_steps, 4),
                 "path": "one pinned H2D copy of all layers Q/K/V, 36 genllm_b200.paged_attention calls (C ABI), one D2H copy of the outputs, host reads the result"},
         "gpu_launches": 2 * args.steps * args.layers,
+        "gather": (args.gather if world > 1 else None),
         "host_enqueue_ms_per_step": round(1e3 * host_enqueue_s / args.steps, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args, world),
@@ -477,6 +503,8 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        if hg is not None:
+            hg.close()
         dist.destroy_process_group()
 
 

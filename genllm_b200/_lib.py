@@ -76,6 +76,14 @@ SIGNATURES = {
     "gkv_append_kv_raw": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), vp, vp, i32, vp], C.c_int),
     "gkv_paged_attention_raw": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), vp, vp, vp, vp, i32, i32,
                                  C.c_float, i32, i32, vp], C.c_int),
+    "gkv_device_alloc": ([C.c_int, C.c_size_t, C.POINTER(vp)], C.c_int),
+    "gkv_device_free": ([C.c_int, vp], C.c_int),
+    "gkv_ipc_export": ([C.c_int, vp, vp], C.c_int),
+    "gkv_ipc_open": ([C.c_int, vp, C.POINTER(vp)], C.c_int),
+    "gkv_ipc_close": ([C.c_int, vp], C.c_int),
+    "gkv_gather_create": ([C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp)], C.c_int),
+    "gkv_gather_destroy": ([vp], C.c_int),
+    "gkv_paged_attention_gather": ([vp, i32, vp, vp, vp, vp, C.c_size_t, i32, C.c_float, i32, vp], C.c_int),
     "gkv_paged_decode_static_scratch": ([C.POINTER(PoolDesc), vp, i32, vp, vp, vp, vp, i32, C.c_float, i32, vp],
                                         C.c_int),
 }

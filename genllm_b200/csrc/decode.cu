@@ -361,16 +361,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
-        // Each warp's state is a partial of its own: split index (CTA, page
-        // slot). The combine kernel merges all of them.
-        if (active) {
+        // Warps that share a kv head (P > 1) merge in registers through shared
+        // memory, in fragment order (lane-major, conflict-free); then the warp
+        // of page slot 0 holds the CTA's partial for its head.
+        if (P > 1) {
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));  // stage buffers are free
+            float* frag = reinterpret_cast<float*>(smem);                 // [warp][36][32]
+            float* mine = frag + warp * 36 * 32 + lane;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) mine[(mt * 4 + i) * 32] = acc[mt][i];
+            mine[32 * 32] = m0;
+            mine[33 * 32] = l0;
+            mine[34 * 32] = m1;
+            mine[35 * 32] = l1;
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+            if (active && pslot == 0) {
+                float M0 = m0, M1 = m1;
+                for (int ps = 1; ps < P; ++ps) {
+                    const float* o = frag + (ps * Hkv + head) * 36 * 32 + lane;
+                    M0 = fmaxf(M0, o[32 * 32]);
+                    M1 = fmaxf(M1, o[34 * 32]);
+                }
+                const float s0 = M0 == -INFINITY ? 0.f : M0, s1 = M1 == -INFINITY ? 0.f : M1;
+                float f0 = exp2_approx(m0 - s0), f1 = exp2_approx(m1 - s1);
+                l0 *= f0;
+                l1 *= f1;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    acc[mt][0] *= f0;
+                    acc[mt][1] *= f1;
+                    acc[mt][2] *= f0;
+                    acc[mt][3] *= f1;
+                }
+                for (int ps = 1; ps < P; ++ps) {
+                    const float* o = frag + (ps * Hkv + head) * 36 * 32 + lane;
+                    const float g0 = exp2_approx(o[32 * 32] - s0), g1 = exp2_approx(o[34 * 32] - s1);
+                    l0 = fmaf(o[33 * 32], g0, l0);
+                    l1 = fmaf(o[35 * 32], g1, l1);
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        acc[mt][0] = fmaf(o[(mt * 4 + 0) * 32], g0, acc[mt][0]);
+                        acc[mt][1] = fmaf(o[(mt * 4 + 1) * 32], g1, acc[mt][1]);
+                        acc[mt][2] = fmaf(o[(mt * 4 + 2) * 32], g0, acc[mt][2]);
+                        acc[mt][3] = fmaf(o[(mt * 4 + 3) * 32], g1, acc[mt][3]);
+                    }
+                }
+                m0 = M0;
+                m1 = M1;
+            }
+        }
+        // The CTA's partial for each query head of this warp's kv head.
+        if (active && pslot == 0) {
             const int Hq = Hkv * G;
-            const int sp = split * P + pslot;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const int n = 2 * t + half;
                 if (n < G) {
-                    const size_t row = (size_t)sp * Hq + head * G + n;
+                    const size_t row = (size_t)split * Hq + head * G + n;
                     float* dst = a.part_acc + row * kHeadDim;
 #pragma unroll
                     for (int mt = 0; mt < 8; ++mt) {
@@ -398,6 +447,8 @@ struct CombineParams {
     int32_t out_dtype;
     int32_t n_q_heads;
     int32_t n_splits;
+    uint32_t* err;
+    GatherLaunch g;
 };
 
 constexpr int kCombineWarps = 8;
@@ -410,8 +461,10 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
     // Only now may the next launch start: a decode step of the same layer
     // reads pages and table entries this step's decode grid wrote, and its
-    // page stream begins before it waits for this grid.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // page stream begins before it waits for this grid. With the fused
+    // gather the trigger comes after this rank's stores and flags are out.
+    const bool gather = c.g.world > 1;
+    if (!gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int hq = blockIdx.x;
     const int lane = threadIdx.x & 31;
     const int d = blockIdx.y * kCombineDims + lane;
@@ -463,7 +516,48 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
             Lt = fmaf(s_l[k], f, Lt);
             At = fmaf(s_a[k][lane], f, At);
         }
-        store_out(c.out, (size_t)hq * kHeadDim + d, At / Lt, c.out_dtype);
+        const float v = At / Lt;
+        if (!gather) {
+            store_out(c.out, (size_t)hq * kHeadDim + d, v, c.out_dtype);
+        } else {
+            for (int r = 0; r < c.g.world; ++r) store_out(c.g.dst[r], (size_t)hq * kHeadDim + d, v, c.out_dtype);
+        }
+    }
+    if (!gather) return;
+    // ---- fused head all-gather: completion protocol ----
+    __threadfence_system();  // this CTA's peer stores are visible before its ticket
+    __syncthreads();
+    __shared__ uint32_t s_last;
+    if (threadIdx.x == 0) {
+        const uint32_t n_ctas = gridDim.x * gridDim.y;
+        s_last = atomicAdd(c.g.ticket, 1u) == n_ctas - 1;
+    }
+    __syncthreads();
+    if (!s_last) {
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        return;
+    }
+    if (threadIdx.x == 0) {
+        *c.g.ticket = 0u;
+        __threadfence_system();
+        for (int r = 0; r < c.g.world; ++r)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(c.g.flag_dst[r]), "r"(c.g.epoch) : "memory");
+    }
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Wait (bounded) until every peer's block for this layer and step arrived.
+    if (threadIdx.x < c.g.world) {
+        const uint32_t* f = c.g.flag_wait + threadIdx.x;
+        const uint64_t t0 = global_timer_ns();
+        uint32_t v;
+        for (uint32_t i = 0;; ++i) {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if ((int32_t)(v - c.g.epoch) >= 0) break;
+            if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(c.err, kErrTimeout);
+                break;
+            }
+        }
     }
 }
 
@@ -480,7 +574,7 @@ bool overlap_enabled() {
 
 cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map, int2* table,
                           const NewPages& np, const Scratch& scratch, const DecodeLaunch& d, int num_sms,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const GatherLaunch* gather) {
     const int Hkv = pool.n_kv_heads;
     if (Hkv > kConsumerWarps) return cudaErrorInvalidValue;
     static unsigned long long configured = 0;
@@ -519,13 +613,13 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     const int n_stages_total = (d.n_pages + P - 1) / P;
     int n_splits = d.n_splits > 0 ? d.n_splits : num_sms;
     if (n_splits > n_stages_total) n_splits = n_stages_total;
-    if (n_splits * P * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / (P * d.n_q_heads);
+    if (n_splits * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / d.n_q_heads;
     if (n_splits < 1) n_splits = 1;
     int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
     if (stages_per_split * P > kMaxSplitPages) {  // very long contexts: more splits than SMs
         stages_per_split = kMaxSplitPages / P;
         n_splits = (n_stages_total + stages_per_split - 1) / stages_per_split;
-        if (n_splits * P * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
+        if (n_splits * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
     }
     p.pages_per_split = stages_per_split * P;
     n_splits = (d.n_pages + p.pages_per_split - 1) / p.pages_per_split;
@@ -547,7 +641,8 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     e = cudaLaunchKernelEx(&dcfg, paged_decode_kernel, k_map, v_map, p);
     if (e != cudaSuccess) return e;
 
-    CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits * P};
+    CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits, scratch.err, {}};
+    if (gather) c.g = *gather;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d.n_q_heads, kHeadDim / kCombineDims);
     cfg.blockDim = dim3(kCombineWarps * 32);

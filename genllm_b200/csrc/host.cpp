@@ -34,6 +34,10 @@ namespace {
 
 thread_local std::string g_last_error;
 
+// Set by gkv_paged_attention_gather around its call of the managed decode
+// path: the fused head all-gather of that one launch.
+thread_local const gkv::GatherLaunch* t_gather = nullptr;
+
 int fail(int status, const char* fmt, ...) {
     char buf[512];
     va_list ap;
@@ -397,7 +401,8 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
         d.n_pages = n_pages;
         d.scale = scale;
         d.n_splits = 0;
-        cudaError_t e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s);
+        cudaError_t e =
+            gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s, t_gather);
         if (e != cudaSuccess) return cuda_fail(e, "decode launch");
         return GKV_OK;
     }
@@ -903,6 +908,132 @@ int gkv_check_device_errors(gkv_manager* m, int32_t layer_id, uint32_t* flags) {
     int st = ready_layer(m, layer_id, &L);
     if (st) return st;
     return gkv_table_check_errors(L->table, flags);
+}
+
+}  // extern "C"
+
+// ============================ multi-GPU head gather ==========================
+
+struct gkv_gather {
+    int device = 0;
+    int world = 0;
+    int rank = 0;
+    int max_layers = 0;
+    void* bases[gkv::kMaxGatherRanks] = {};
+    uint32_t* flags[gkv::kMaxGatherRanks] = {};
+    uint32_t* tickets = nullptr;  // [max_layers], zero between launches
+    std::vector<uint32_t> epochs;  // calls so far per layer
+};
+
+extern "C" {
+
+int gkv_device_alloc(int device, size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return fail(GKV_ERR_INVALID, "bad arguments");
+    DeviceGuard g(device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", device);
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    return e == cudaSuccess ? GKV_OK : cuda_fail(e, "gkv_device_alloc");
+}
+
+int gkv_device_free(int device, void* ptr) {
+    DeviceGuard g(device);
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? GKV_OK : cuda_fail(e, "gkv_device_free");
+}
+
+int gkv_ipc_export(int device, const void* dev_ptr, void* handle) {
+    if (!dev_ptr || !handle) return fail(GKV_ERR_INVALID, "bad arguments");
+    DeviceGuard g(device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    std::memcpy(handle, &h, sizeof h);
+    return GKV_OK;
+}
+
+int gkv_ipc_open(int device, const void* handle, void** dev_ptr) {
+    if (!dev_ptr || !handle) return fail(GKV_ERR_INVALID, "bad arguments");
+    DeviceGuard g(device);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? GKV_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int gkv_ipc_close(int device, void* dev_ptr) {
+    DeviceGuard g(device);
+    cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    return e == cudaSuccess ? GKV_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int gkv_gather_create(int device, int world, int rank, int max_layers, void* const* out_bases,
+                      uint32_t* const* flag_bases, gkv_gather** out) {
+    if (!out || world < 2 || world > gkv::kMaxGatherRanks || rank < 0 || rank >= world || max_layers < 1 ||
+        !out_bases || !flag_bases)
+        return fail(GKV_ERR_INVALID, "gkv_gather_create: bad arguments");
+    for (int r = 0; r < world; ++r)
+        if (!out_bases[r] || !flag_bases[r]) return fail(GKV_ERR_INVALID, "null base for rank %d", r);
+    DeviceGuard g(device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", device);
+    auto* gg = new gkv_gather();
+    gg->device = device;
+    gg->world = world;
+    gg->rank = rank;
+    gg->max_layers = max_layers;
+    for (int r = 0; r < world; ++r) {
+        gg->bases[r] = out_bases[r];
+        gg->flags[r] = flag_bases[r];
+    }
+    gg->epochs.assign(max_layers, 0);
+    cudaError_t e = cudaMalloc(&gg->tickets, sizeof(uint32_t) * (size_t)max_layers);
+    if (e == cudaSuccess) e = cudaMemset(gg->tickets, 0, sizeof(uint32_t) * (size_t)max_layers);
+    if (e != cudaSuccess) {
+        cudaFree(gg->tickets);
+        delete gg;
+        return cuda_fail(e, "gkv_gather_create");
+    }
+    *out = gg;
+    return GKV_OK;
+}
+
+int gkv_gather_destroy(gkv_gather* gg) {
+    if (!gg) return GKV_OK;
+    DeviceGuard g(gg->device);
+    cudaFree(gg->tickets);
+    delete gg;
+    return GKV_OK;
+}
+
+int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, const void* K, const void* V,
+                               gkv_gather* gg, size_t out_offset, int32_t n_q_heads, float scale, int32_t out_dtype,
+                               gkv_stream_t stream) {
+    if (!gg) return fail(GKV_ERR_INVALID, "null gather");
+    if (layer_id < 0 || layer_id >= gg->max_layers) return fail(GKV_ERR_INVALID, "layer %d beyond the gather's %d",
+                                                             layer_id, gg->max_layers);
+    if (m->device != gg->device) return fail(GKV_ERR_INVALID, "manager and gather on different devices");
+    const Layer* L = find_layer(m, layer_id);
+    if (!L || !L->reserved) return fail(GKV_ERR_STATE, "layer %d not reserved", layer_id);
+    const size_t esize = out_dtype == GKV_F32 ? 4 : 2;
+    const size_t block = (size_t)n_q_heads * 128 * esize;
+    if (out_offset % 16 != 0) return fail(GKV_ERR_INVALID, "out_offset must be 16-byte aligned");
+    gkv::GatherLaunch gl{};
+    gl.world = gg->world;
+    gl.rank = gg->rank;
+    for (int r = 0; r < gg->world; ++r) {
+        gl.dst[r] = static_cast<char*>(gg->bases[r]) + out_offset + (size_t)gg->rank * block;
+        gl.flag_dst[r] = gg->flags[r] + (size_t)layer_id * gg->world + gg->rank;
+    }
+    gl.flag_wait = gg->flags[gg->rank] + (size_t)layer_id * gg->world;
+    gl.epoch = gg->epochs[layer_id] + 1;
+    gl.ticket = gg->tickets + layer_id;
+    // The managed decode path, with this gather attached to its combine launch.
+    t_gather = &gl;
+    const int st = gkv_paged_attention(m, layer_id, Q, K, V, gl.dst[gg->rank], 1, n_q_heads, 1, 128, L->n_kv_heads,
+                                       scale, 1, n_q_heads / L->n_kv_heads, L->dtype, out_dtype, stream);
+    t_gather = nullptr;
+    if (st == GKV_OK) gg->epochs[layer_id] = gl.epoch;
+    return st;
 }
 
 }  // extern "C"

@@ -51,12 +51,29 @@ struct DecodeLaunch {
     int32_t n_splits;       // 0 = choose
 };
 
+// Head all-gather fused into the split combine (multi-GPU KV-head sharding):
+// every rank's combine stores its query-head block into every rank's full
+// output buffer over NVLink peer memory (plain stores), then publishes the
+// step's call count in each peer's flag slot and waits (bounded) until all
+// peers' slots for this layer reach it.
+constexpr int kMaxGatherRanks = 8;
+struct GatherLaunch {
+    int32_t world;                        // 0 = no gather
+    int32_t rank;
+    void* dst[kMaxGatherRanks];           // this rank's head block in rank r's full buffer
+    uint32_t* flag_dst[kMaxGatherRanks];  // this rank's flag slot (this layer) on rank r
+    const uint32_t* flag_wait;            // this layer's slots on this rank, world entries
+    uint32_t epoch;                       // call count of this layer, 1-based
+    uint32_t* ticket;                     // CTA completion counter (zero between launches)
+};
+
 // Fused decode step: append one token's K/V, GQA-grouped split-K
 // flash-decoding over the block table (k_map/v_map: the pool's 128-byte
 // swizzled maps), then the split combine. Returns the CUDA error.
 cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map,
                           int2* table, const NewPages& np, const Scratch& scratch,
-                          const DecodeLaunch& d, int num_sms, cudaStream_t stream);
+                          const DecodeLaunch& d, int num_sms, cudaStream_t stream,
+                          const GatherLaunch* gather = nullptr);
 
 // Scatter tokens [p_begin, p_end) of K/V ([Hkv][src_len][128]) to positions
 // n_prior + p, and publish np's entries to the table. With p_begin == p_end

@@ -79,11 +79,10 @@ extern "C" int gkv_paged_decode_static_scratch(const gkv_pool_desc* pool, const 
         base = g_addr[dev];
         sms = g_sms[dev];
     }
-    // Splits are capped so that the partial rows (splits x warps sharing a
-    // head x query heads) fit the static rows.
-    const int pages_per_stage = 8 / pool->n_kv_heads;
+    // Splits are capped so that the partial rows (splits x query heads) fit
+    // the static rows.
     int n_splits = sms;
-    if (n_splits * pages_per_stage * n_q_heads > kStaticRows) n_splits = kStaticRows / (pages_per_stage * n_q_heads);
+    if (n_splits * n_q_heads > kStaticRows) n_splits = kStaticRows / n_q_heads;
     if (n_splits < 1) return fail(GKV_ERR_UNSUPPORTED, "too many query heads for the static scratch");
     if ((long long)n_pages > 1000LL * n_splits)
         return fail(GKV_ERR_INVALID, "context longer than the static scratch supports");

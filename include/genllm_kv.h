@@ -229,6 +229,44 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
                             void* out, int32_t n_q_heads, int32_t seq_len, float scale,
                             int32_t causal, int32_t out_dtype, gkv_stream_t stream);
 
+/* ======================= multi-GPU head all-gather ======================== */
+
+/* KV-head sharding across the GPUs of one node (the reference has no
+ * multi-GPU attention; its layers move between devices through host copies,
+ * src/backend/cuda/memcpy.cu:29-44). Each rank's manager holds Hkv / N heads;
+ * after a decode step every rank needs all N head blocks of the output. This
+ * tier writes them there from inside the split-combine kernel over NVLink
+ * (plain peer stores into memory opened with CUDA IPC), instead of a
+ * separate all-gather launch.
+ *
+ * Device buffers to share between processes come from gkv_device_alloc
+ * (zero-filled cudaMalloc); gkv_ipc_export / gkv_ipc_open / gkv_ipc_close
+ * move them across processes (64-byte handles, exchanged by the caller). */
+int gkv_device_alloc(int device, size_t bytes, void** ptr);
+int gkv_device_free(int device, void* ptr);
+int gkv_ipc_export(int device, const void* dev_ptr, void* handle /* 64 bytes */);
+int gkv_ipc_open(int device, const void* handle, void** dev_ptr);
+int gkv_ipc_close(int device, void* dev_ptr);
+
+typedef struct gkv_gather gkv_gather;
+
+/* out_bases[r]: rank r's full-output region as mapped in this process (its
+ * own region for r == rank); flag_bases[r]: rank r's flag array of
+ * max_layers * world uint32, zero-filled, mapped likewise. */
+int gkv_gather_create(int device, int world, int rank, int max_layers, void* const* out_bases,
+                      uint32_t* const* flag_bases, gkv_gather** out);
+int gkv_gather_destroy(gkv_gather* g);
+
+/* One decode step of this rank's heads (as gkv_paged_attention with
+ * seq_len 1, causal), whose [n_q_heads][128] output block lands in EVERY
+ * rank's region at out_offset + rank * n_q_heads * 128 * elem bytes. The
+ * launch completes only once all ranks' blocks for this layer and step have
+ * arrived in this rank's region (a bounded wait, 1 s; on timeout the device
+ * error word gets bit 1). Every rank must make the same sequence of calls. */
+int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, const void* K,
+                               const void* V, gkv_gather* g, size_t out_offset, int32_t n_q_heads,
+                               float scale, int32_t out_dtype, gkv_stream_t stream);
+
 /* ======================= no-allocation decode ============================ */
 
 /* No counterpart in the reference. One fused decode step (append the token
@@ -243,7 +281,7 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
  *   every page up to and including the one that receives the new token.
  *   Q [Hq][128], K and V [Hkv][128] (this step's token), out [Hq][128].
  * Limits: head_dim 128, bf16 pages, 1-8 kv heads, group size 1/2/4/8; the
- * fixed scratch holds 4096 partial rows (splits x (8 / Hkv) x Hq), so larger
+ * fixed scratch holds 4096 partial rows (splits x Hq), so larger
  * Hq gets fewer splits; context <= 1000 pages per split; larger requests return GKV_ERR_INVALID / GKV_ERR_UNSUPPORTED.
  * The first call on a device looks up the scratch address on the current
  * device; make that first call before any stream capture. All calls share
