@@ -76,6 +76,9 @@ struct DecodeParams {
     int32_t new_first;
     int32_t new_n;
     float qscale;  // softmax scale * log2(e)
+#ifdef GKV_PROBE_TIMELINE
+    int32_t probe_slot;
+#endif
     int2 new_ids[kMaxNewPagesPerLaunch];
 };
 
@@ -117,14 +120,14 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 }
 
 #ifdef GKV_PROBE_TIMELINE
-__device__ unsigned long long g_probe_tl[4096 * 8];
+__device__ unsigned long long g_probe_tl[8 * 4096 * 8];
 #define PROBE_T(k) \
-    if (threadIdx.x == 0) g_probe_tl[blockIdx.x * 8 + (k)] = global_timer_ns();
+    if (threadIdx.x == 0) g_probe_tl[(a.probe_slot * 4096 + blockIdx.x) * 8 + (k)] = global_timer_ns();
 #else
 #define PROBE_T(k)
 #endif
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
                         const DecodeParams a) {
     extern __shared__ uint8_t smem_raw[];
@@ -449,16 +452,26 @@ struct CombineParams {
     int32_t n_splits;
     uint32_t* err;
     GatherLaunch g;
+#ifdef GKV_PROBE_TIMELINE
+    int32_t probe_slot;
+#endif
 };
 
-constexpr int kCombineWarps = 8;
+constexpr int kCombineWarps = 8;  // 8 warps x 80 registers fit beside a decode CTA (96 registers) on every SM
 constexpr int kCombineDims = 32;  // dims per CTA (one per lane)
 
 // Grid (Hq, 128 / 32): warp w of a CTA folds splits w, w + 8, ... for the
 // CTA's 32 dims (one per lane, 128-byte coalesced rows), then the 8 warps
 // merge through shared memory.
 __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_kernel(const CombineParams c) {
+#ifdef GKV_PROBE_TIMELINE
+#define PROBE_C(k) if (threadIdx.x == 0) g_probe_tl[(c.probe_slot * 4096 + 2048 + blockIdx.y * gridDim.x + blockIdx.x) * 8 + (k)] = global_timer_ns();
+#else
+#define PROBE_C(k)
+#endif
+    PROBE_C(0);
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
+    PROBE_C(1);
     // Only now may the next launch start: a decode step of the same layer
     // reads pages and table entries this step's decode grid wrote, and its
     // page stream begins before it waits for this grid. With the fused
@@ -516,6 +529,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
             Lt = fmaf(s_l[k], f, Lt);
             At = fmaf(s_a[k][lane], f, At);
         }
+        PROBE_C(2);
         const float v = At / Lt;
         if (!gather) {
             store_out(c.out, (size_t)hq * kHeadDim + d, v, c.out_dtype);
@@ -584,6 +598,13 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     if (dev >= 64 || !(configured & (1ull << dev))) {
         e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
         if (e != cudaSuccess) return e;
+        // Both kernels ask for the largest shared-memory carveout, so that an
+        // SM running combine CTAs can take the next decode CTA without
+        // reconfiguring (which would wait for the combine CTAs to drain).
+        e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(paged_decode_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
     DecodeParams p;
@@ -606,6 +627,10 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     p.qscale = d.scale * 1.4426950408889634f;
     p.new_first = np.first;
     p.new_n = np.n;
+#ifdef GKV_PROBE_TIMELINE
+    static int probe_counter = 0;
+    p.probe_slot = probe_counter++ % 8;
+#endif
     for (int i = 0; i < np.n; ++i) p.new_ids[i] = np.ids[i];
 
     // One CTA per SM; each split a whole number of stages.
@@ -643,6 +668,9 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
 
     CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits, scratch.err, {}};
     if (gather) c.g = *gather;
+#ifdef GKV_PROBE_TIMELINE
+    c.probe_slot = p.probe_slot;
+#endif
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d.n_q_heads, kHeadDim / kCombineDims);
     cfg.blockDim = dim3(kCombineWarps * 32);
