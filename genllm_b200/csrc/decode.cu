@@ -188,21 +188,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
 
     int2* ids = reinterpret_cast<int2*>(smem + kOffIds);
-    for (int i = threadIdx.x; i < p1 - p0; i += kThreads) ids[i] = checked(i);
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == kConsumerWarps * 32) {
+        // Producer: barriers, then stage 0 straight from the table while the
+        // other threads cache the split's ids (saves one table round trip
+        // on the first data).
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
         fence_mbar_init();
+        if (n_stages > 0) issue_stage(0, checked);
     }
+    for (int i = threadIdx.x; i < p1 - p0; i += kThreads) ids[i] = checked(i);
     __syncthreads();
     PROBE_T(1);
 
     if (warp == kConsumerWarps) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            for (int i = 0; i < n_stages; ++i) {
+            for (int i = 1; i < n_stages; ++i) {
                 const int st = i % kStages;
                 if (i >= kStages && !mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1))
                     atomicOr(a.err, kErrTimeout);
