@@ -106,3 +106,20 @@ __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.
 
 }  // namespace tc
 }  // namespace gkv
+
+namespace gkv {
+namespace tc {
+// 2 columns of 32-bit for this thread's TMEM lane.
+__device__ __forceinline__ void st2(uint32_t taddr, float a, float b) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(__float_as_uint(a)),
+                 "r"(__float_as_uint(b))
+                 : "memory");
+}
+__device__ __forceinline__ void ld2(uint32_t taddr, float& a, float& b) {
+    uint32_t x, y;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(x), "=r"(y) : "r"(taddr));
+    a = __uint_as_float(x);
+    b = __uint_as_float(y);
+}
+}  // namespace tc
+}  // namespace gkv
