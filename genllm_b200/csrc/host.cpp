@@ -133,6 +133,14 @@ bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMa
            encode(v_map, pool.v_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
 }
 
+bool encode_pool_run_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)pool.n_kv_heads, (cuuint64_t)pool.pool_pages * 16};
+    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)pool.n_kv_heads * kHeadDim * 2};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)kRunSlots};
+    return encode(k_map, pool.k_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why) &&
+           encode(v_map, pool.v_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
+}
+
 bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, CUtensorMap* q_map,
                         const char** why) {
     cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)seq_len, (cuuint64_t)n_q_heads};
@@ -158,6 +166,9 @@ struct gkv_table {
     int32_t map_heads = -1;
     CUtensorMap k_map_sw;   // box {64 dims, 1 head, 16 slots}, 128-byte swizzle
     CUtensorMap v_map_sw;
+    CUtensorMap k_map_run;  // box {64 dims, 1 head, 128 slots}: 8 pages with consecutive ids
+    CUtensorMap v_map_run;
+    bool runs = false;      // run maps valid (the pool holds at least 8 pages)
 };
 
 namespace {
@@ -193,6 +204,9 @@ int table_maps(gkv_table* t, const gkv_pool_desc* pool) {
                      pool->pool_pages, pool->n_kv_heads};
     const char* why = nullptr;
     if (!gkv::encode_pool_maps_sw128(pv, &t->k_map_sw, &t->v_map_sw, &why))
+        return fail(GKV_ERR_CUDA, "%s", why);
+    t->runs = pool->pool_pages * 16 >= gkv::kRunSlots;
+    if (t->runs && !gkv::encode_pool_run_maps_sw128(pv, &t->k_map_run, &t->v_map_run, &why))
         return fail(GKV_ERR_CUDA, "%s", why);
     t->map_k_base = pool->k_base;
     t->map_v_base = pool->v_base;
@@ -425,7 +439,9 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
         CUtensorMap q_map;
         const char* why = nullptr;
         if (!gkv::encode_q_map_sw128(pl.q, n_q_heads, seq_len, &q_map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
-        e = gkv::launch_prefill_tc(pv, q_map, t->k_map_sw, t->v_map_sw, t->d_table, pl, t->scratch.err, t->num_sms, s);
+        const gkv::PoolMaps maps{t->k_map_sw, t->v_map_sw, t->runs ? t->k_map_run : t->k_map_sw,
+                                 t->runs ? t->v_map_run : t->v_map_sw, t->runs};
+        e = gkv::launch_prefill_tc(pv, q_map, maps, t->d_table, pl, t->scratch.err, t->num_sms, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
     return GKV_OK;

@@ -102,13 +102,22 @@ void set_last_error(const char* msg);
 // swizzle, box {64, 1, 16}; the chunk's Q [Hq][S][128], box {64, 128, 1}.
 bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map,
                             const char** why);
+// The same with box {64, 1, 128}: one copy covers a run of 8 pages whose ids
+// are consecutive (the common case for a sequence appended in one go).
+constexpr int kRunSlots = 128;
+bool encode_pool_run_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map,
+                                const char** why);
+struct PoolMaps {
+    CUtensorMap k, v;          // one page per copy
+    CUtensorMap k_run, v_run;  // 8 consecutive pages per copy
+    bool runs;                 // k_run / v_run usable
+};
 bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, CUtensorMap* q_map,
                         const char** why);
 
 // Attention of a chunk of seq_len queries over the cached pages (the chunk's
 // own K/V already appended), on the tensor cores.
-cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map,
-                              const CUtensorMap& k_map, const CUtensorMap& v_map,
+cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const PoolMaps& maps,
                               const int2* table, const PrefillLaunch& p, uint32_t* err,
                               int num_sms, cudaStream_t stream);
 

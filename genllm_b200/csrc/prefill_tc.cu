@@ -42,13 +42,16 @@ constexpr int kPagesPerTile = kBN / kPageSlots;
 constexpr uint32_t kHalf = 128 * 128;          // one 64-dim half of a 128-row tile: 16 KiB
 constexpr uint32_t kTile = 2 * kHalf;          // 32 KiB
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kTile;      // 2 stages
-constexpr uint32_t kOffV = kOffK + 2 * kTile;  // 2 stages
-constexpr uint32_t kOffP = kOffV + 2 * kTile;   // P as bf16 hi part
-constexpr uint32_t kOffPlo = kOffP + kTile;     // and lo part (P - hi), for fp32-level PV accuracy
-constexpr uint32_t kOffBar = kOffPlo + kTile;
-constexpr uint32_t kSmemBytes = kOffBar + 128 + 1024;  // + 8 barriers, TMEM slot, alignment slack
-constexpr uint32_t kTmemCols = 512;            // S: two buffers [0, 256), O: [256, 384)
+constexpr int kStages = 3;                     // K and V tiles in flight
+constexpr uint32_t kOffK = kOffQ + kTile;
+constexpr uint32_t kOffV = kOffK + kStages * kTile;
+constexpr uint32_t kOffBar = kOffV + kStages * kTile;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, TMEM slot, alignment slack
+static_assert((6 + 4 * kStages) * 8 + 4 <= 256, "barriers and the TMEM slot fit their 256 bytes");
+// TMEM columns: S/P of two tiles [0, 256), O [256, 384), Q as the A operand
+// of Q K^T [384, 448) (bf16 pairs), max/sum exchange [448, 452).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256, kColQ = 384, kColX = 448;
 
 struct TcParams {
     const int2* table;
@@ -62,38 +65,89 @@ struct TcParams {
     int32_t n_pages;
     int32_t pool_pages;
     int32_t causal;
+    int32_t runs;  // k_run / v_run maps usable
     float qscale;  // softmax scale * log2(e)
 };
 
 constexpr int kConsumerThreads = 256;               // 8 warps: 2 threads per query row
-constexpr int kLoadWarp = kConsumerThreads / 32;   // issues the TMA loads
-constexpr int kMmaWarp = kLoadWarp + 1;            // issues the tcgen05 MMAs
-constexpr int kThreadsTc = kConsumerThreads + 64;
+constexpr int kLoadWarp = kConsumerThreads / 32;   // issues the K loads (warp + 1: the V loads)
+constexpr int kMmaWarp = kLoadWarp + 2;            // issues the tcgen05 MMAs
+constexpr int kThreadsTc = kConsumerThreads + 96;
+constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
 
 #ifdef GKV_PROBE_TIMELINE
 // Measurement builds only: per-tile phase clocks of threads 0 and 128 of the
 // first CTA of the grid.
-__device__ long long g_probe_pf[2 * 128 * 8];
+__device__ long long g_probe_pf[2 * 128 * 16];
+__device__ long long g_probe_mma[128 * 4];
+__device__ long long g_probe_ld[128 * 8];
+#define PROBE_LD(k)                                                                                  \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 128) g_probe_ld[j * 8 + (k)] = clock64();
+#define PROBE_MMA(k)                                                                                 \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 128) g_probe_mma[j * 4 + (k)] = clock64();
 #define PROBE_PF(k)                                                                                  \
     if ((tid & 127) == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 128)        \
-        g_probe_pf[((tid >> 7) * 128 + j) * 8 + (k)] = clock64();
+        g_probe_pf[((tid >> 7) * 128 + j) * 16 + (k)] = clock64();
 #else
 #define PROBE_PF(k)
+#define PROBE_MMA(k)
+#define PROBE_LD(k)
 #endif
+
+// How a tile's 8 pages are copied: 0 = page by page; 1 = one run of
+// ascending consecutive ids (K and V alike); 2 = one run of descending ids
+// (what the LIFO free list hands out after a reset), whose copy lands the
+// pages in reverse order. Lanes 0-7 of the calling warp hold entry `lane` of
+// the tile; every lane gets the same answer. The load warps evaluate the same
+// rule on their private copy of the entries (tile_mode_regs), so producers
+// and consumers agree on the layout of every stage.
+__device__ __forceinline__ int tile_mode_warp(int2 e, int lane, int pool_pages, int runs) {
+    const int x0 = __shfl_sync(0xFFFFFFFFu, e.x, 0), y0 = __shfl_sync(0xFFFFFFFFu, e.y, 0);
+    const bool in = lane < kPagesPerTile;
+    const bool asc = __all_sync(0xFFFFFFFFu, !in || (e.x == x0 + lane && e.y == y0 + lane));
+    const bool desc = __all_sync(0xFFFFFFFFu, !in || (e.x == x0 - lane && e.y == y0 - lane));
+    if (!runs) return 0;
+    if (asc && x0 >= 0 && y0 >= 0 && x0 + kPagesPerTile <= pool_pages && y0 + kPagesPerTile <= pool_pages) return 1;
+    if (desc && x0 - (kPagesPerTile - 1) >= 0 && y0 - (kPagesPerTile - 1) >= 0 && x0 < pool_pages && y0 < pool_pages)
+        return 2;
+    return 0;
+}
+__device__ __forceinline__ int tile_mode_regs(const int2 (&e)[kPagesPerTile], int pool_pages, int runs) {
+    const int x0 = e[0].x, y0 = e[0].y;
+    bool asc = true, desc = true;
+#pragma unroll
+    for (int i = 1; i < kPagesPerTile; ++i) {
+        asc = asc && e[i].x == x0 + i && e[i].y == y0 + i;
+        desc = desc && e[i].x == x0 - i && e[i].y == y0 - i;
+    }
+    if (!runs) return 0;
+    if (asc && x0 >= 0 && y0 >= 0 && x0 + kPagesPerTile <= pool_pages && y0 + kPagesPerTile <= pool_pages) return 1;
+    if (desc && x0 - (kPagesPerTile - 1) >= 0 && y0 - (kPagesPerTile - 1) >= 0 && x0 < pool_pages && y0 < pool_pages)
+        return 2;
+    return 0;
+}
+// Key (within the tile) held by smem row / S column c of a tile copied in `mode`.
+__device__ __forceinline__ int tile_key(int c, int mode) {
+    return mode == 2 ? (((kPagesPerTile - 1 - (c >> 4)) << 4) | (c & 15)) : c;
+}
 
 __global__ void __launch_bounds__(kThreadsTc, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
-                      const __grid_constant__ CUtensorMap v_map, const TcParams a) {
+                      const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap k_run,
+                      const __grid_constant__ CUtensorMap v_run, const TcParams a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kOffBar);
-    uint64_t* bar_k = bar_q + 1;  // [2] K tile landed
-    uint64_t* bar_v = bar_q + 3;  // [2] V tile landed
-    uint64_t* bar_s = bar_q + 5;  // [2] S = Q K^T of a tile done
-    uint64_t* bar_o = bar_q + 7;  // P V of a tile done (consumers)
-    uint64_t* bar_vfree = bar_q + 8;  // [2] P V of a tile done (load warp: V buffer free)
-    uint64_t* bar_p = bar_q + 10;     // consumers: P of a tile written (and S of it read)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + 11);
+    uint64_t* bar_k = bar_q + 1;             // [kStages] K tile landed
+    uint64_t* bar_v = bar_k + kStages;       // [kStages] V tile landed
+    uint64_t* bar_kfree = bar_v + kStages;   // [kStages] Q K^T of the stage's tile done
+    uint64_t* bar_vfree = bar_kfree + kStages;  // [kStages] P V of the stage's tile done
+    uint64_t* bar_s = bar_vfree + kStages;   // [2] S of a tile in its TMEM buffer
+    uint64_t* bar_o = bar_s + 2;             // P V of a tile done (in issue order)
+    uint64_t* bar_p = bar_o + 1;             // consumers: P of a tile written (and S of it read)
+    uint64_t* bar_qt = bar_p + 1;            // consumers: Q copied into TMEM
+    constexpr int kNumBars = 6 + 4 * kStages;  // q, k, v, kfree, vfree, s[2], o, p, qt
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + kNumBars);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -117,7 +171,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         tc::tmem_relinquish();
     }
     if (tid == 0) {
-        for (int b = 0; b < 11; ++b) mbar_init(bar_q + b, 1);
+        for (int b = 0; b < kNumBars; ++b) mbar_init(bar_q + b, 1);
         fence_mbar_init();
     }
     tc::fence_before_sync();
@@ -125,14 +179,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
-    const uint32_t t_o = tmem + lane_base + 256;             // O columns [256, 384)
+    const uint32_t t_o = tmem + lane_base + kColO;           // this warp's lanes of O
 
-    const uint32_t sQ = smem_addr(smem + kOffQ);
     const uint32_t sK = smem_addr(smem + kOffK);
     const uint32_t sV = smem_addr(smem + kOffV);
-    const uint32_t sP = smem_addr(smem + kOffP);
-    const uint32_t sPlo = smem_addr(smem + kOffPlo);
+    // Q is read once; K and V tiles are read again by the CTAs of the other
+    // query tiles and heads of the group, so they keep normal L2 priority.
     const uint64_t pol = l2_policy_evict_first();
+    uint64_t pol_kv;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol_kv));
 
     // Page ids of tile j: 8 independent table loads (one latency, not 8),
     // fetched by the issuing thread a tile before they are needed.
@@ -144,12 +199,26 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             e[i] = a.table[lp];
         }
     };
-    // Stage tile j's K (which = 0) or V (which = 1) into buffer (j & 1): 8
-    // pages x 2 halves, one TMA box {64, 1, 16} each.
+    // Stage tile j's K (which = 0) or V (which = 1) into stage j % kStages.
+    // Eight pages with consecutive ids are one run: two copies (one per
+    // 64-dim half) with box {64, 1, 128} instead of 8 pages x 2 halves of box
+    // {64, 1, 16}. A TMA copy costs its issuing thread about the same whatever
+    // its size, so runs cut the load warps' issue time per tile by 8x. A
+    // descending run lands its pages in reverse order (tile_key).
     auto issue = [&](int j, int which, const int2 (&ids)[kPagesPerTile]) {
-        const int st = j & 1;
+        const int st = j % kStages;
         uint64_t* bar = which ? &bar_v[st] : &bar_k[st];
         mbar_arrive_expect_tx(bar, kTile);
+        const int mode = tile_mode_regs(ids, a.pool_pages, a.runs);
+        if (mode != 0) {
+            const int first = which ? ids[0].y : ids[0].x;
+            const int low = mode == 1 ? first : first - (kPagesPerTile - 1);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+                tma_load_3d(smem + (which ? kOffV : kOffK) + st * kTile + hf * kHalf, which ? &v_run : &k_run, bar,
+                            hf * 64, h, low * kPageSlots, pol_kv);
+            return;
+        }
 #pragma unroll
         for (int i = 0; i < kPagesPerTile; ++i) {
             int2 e = ids[i];
@@ -161,10 +230,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             for (int hf = 0; hf < 2; ++hf) {
                 if (which == 0)
                     tma_load_3d(smem + kOffK + st * kTile + hf * kHalf + i * 2048, &k_map, bar, hf * 64, h,
-                                e.x * kPageSlots, pol);
+                                e.x * kPageSlots, pol_kv);
                 else
                     tma_load_3d(smem + kOffV + st * kTile + hf * kHalf + i * 2048, &v_map, bar, hf * 64, h,
-                                e.y * kPageSlots, pol);
+                                e.y * kPageSlots, pol_kv);
             }
         }
     };
@@ -180,51 +249,78 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
         if (ok && !mbar_wait_bounded(bar, parity)) ok = false;
     };
-    // S(j) = Q K(j)^T into TMEM columns [(j & 1) * 128, +128).
+    // S(j) = Q K(j)^T into TMEM columns [(j & 1) * 128, +128), Q read from
+    // TMEM: only K streams from shared memory, whose bandwidth bounds an
+    // N = 128 MMA with both operands there.
+    // The MMA warp runs converged; one elected lane issues. Descriptors are
+    // built once and stepped by adding the byte offset / 16 to their address
+    // field (smem addresses stay below 256 KiB, so the 14-bit field cannot
+    // carry). A tight issue sequence keeps the tensor pipe fed: each
+    // m128n128k16 MMA takes 64 cycles, about what loose issue code spends
+    // between two MMAs.
+    const uint64_t desc_k0 = tc::smem_desc_sw128(sK, 16, 1024);
+    const uint64_t desc_v0 = tc::smem_desc_sw128(sV, kHalf, 1024);
     auto issue_qk = [&](int j) {
-        const int st = j & 1;
-        wait(&bar_k[st], (j >> 1) & 1);
+        const int sb = j & 1, st = j % kStages;
+        wait(&bar_k[st], (j / kStages) & 1);
+        PROBE_LD(6);
         tc::fence_after_sync();
+        if (tc::elect_one()) {
+            const uint64_t dk = desc_k0 + ((st * kTile) >> 4);
+            const uint32_t d = tmem + sb * 128;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            tc::mma_bf16(tmem + st * 128, tc::smem_desc_sw128(sQ + off, 16, 1024),
-                         tc::smem_desc_sw128(sK + st * kTile + off, 16, 1024), kIdescQK, kk > 0);
+            for (int kk = 0; kk < 8; ++kk)
+                tc::mma_bf16_ts(d, tmem + kColQ + kk * 8, dk + ((((kk >> 2) * kHalf) + (kk & 3) * 32) >> 4), kIdescQK,
+                                kk > 0);
+            tc::commit(&bar_s[sb]);
+            tc::commit(&bar_kfree[st]);
         }
-        tc::commit(&bar_s[st]);
+        __syncwarp();
     };
 
-    // P(j) V(j) into the O columns [256, 384), both bf16 terms of P.
+    // P(j) V(j) into the O columns [256, 384), both bf16 terms of P, with P
+    // read from TMEM (where it replaced S(j)).
     auto issue_pv = [&](int j) {
-        const int st = j & 1;
+        const int sb = j & 1, st = j % kStages;
+        if (tc::elect_one()) {
+            const uint64_t dv = desc_v0 + ((st * kTile) >> 4);
+            const uint32_t p = tmem + sb * 128;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t po = (kk >> 2) * kHalf + (kk & 3) * 32;
-            const uint64_t db = tc::smem_desc_sw128(sV + st * kTile + kk * 2048, kHalf, 1024);
-            tc::mma_bf16(tmem + 256, tc::smem_desc_sw128(sP + po, 16, 1024), db, kIdescPV, j > 0 || kk > 0);
-            tc::mma_bf16(tmem + 256, tc::smem_desc_sw128(sPlo + po, 16, 1024), db, kIdescPV, true);
+            for (int kk = 0; kk < 8; ++kk) {
+                tc::mma_bf16_ts(tmem + kColO, p + kk * 8, dv + ((kk * 2048) >> 4), kIdescPV, j > 0 || kk > 0);
+                tc::mma_bf16_ts(tmem + kColO, p + 64 + kk * 8, dv + ((kk * 2048) >> 4), kIdescPV, true);
+            }
+            tc::commit(bar_o);
+            tc::commit(&bar_vfree[st]);
         }
-        tc::commit(bar_o);
-        tc::commit(&bar_vfree[st]);
+        __syncwarp();
     };
 
     // Warp-specialised software pipeline. The consumer warps (0-7) run the
     // softmax of tile j while the tensor cores compute S of tile j+1 (two S
-    // buffers in TMEM). The load warp issues K(j) once QK(j-2) is done and
-    // V(j) once PV(j-2) is done; the MMA warp issues QK(0), QK(1), then per
-    // tile PV(j) once the consumers have written P(j), followed by QK(j+2)
-    // into the S buffer the consumers just finished reading.
+    // buffers in TMEM). One load warp issues K(j) once QK(j-3) has freed its
+    // stage, another V(j) once PV(j-3) has; the MMA warp
+    // issues QK(0), QK(1), then per tile PV(j) once the consumers have written
+    // P(j), followed by QK(j+2) into the TMEM buffer P(j) occupied.
     if (warp == kMmaWarp) {
-        if ((tid & 31) == 0 && n_tiles > 0) {
-            wait(bar_q, 0);
+        if (n_tiles > 0) {
+            wait(bar_qt, 0);
+            tc::fence_after_sync();
             issue_qk(0);
             if (n_tiles > 1) issue_qk(1);
             for (int j = 0; j < n_tiles && ok; ++j) {
                 wait(bar_p, j & 1);
+                PROBE_MMA(0);
                 tc::fence_after_sync();
                 if (!ok) break;
                 issue_pv(j);
-                if (j + 2 < n_tiles) issue_qk(j + 2);
+                if (j + 2 < n_tiles) {
+                    wait(bar_o, j & 1);  // QK(j+2) overwrites P(j) in TMEM
+                    PROBE_MMA(1);
+                    tc::fence_after_sync();
+                    issue_qk(j + 2);
+                    PROBE_MMA(2);
+                }
             }
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
@@ -237,26 +333,30 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         __syncthreads();
         return;
     }
-    if (warp == kLoadWarp) {
-        if ((tid & 31) == 0) {
-            mbar_arrive_expect_tx(bar_q, kTile);
-            tma_load_3d(smem + kOffQ, &q_map, bar_q, 0, q0, hq, pol);
-            tma_load_3d(smem + kOffQ + kHalf, &q_map, bar_q, 64, q0, hq, pol);
+    if (warp == kLoadWarp || warp == kLoadWarp + 1) {
+        const int lane = tid & 31;
+        if (lane == 0) {
+            const int which = warp - kLoadWarp;  // 0: K, 1: V
+            if (which == 0) {
+                mbar_arrive_expect_tx(bar_q, kTile);
+                tma_load_3d(smem + kOffQ, &q_map, bar_q, 0, q0, hq, pol);
+                tma_load_3d(smem + kOffQ + kHalf, &q_map, bar_q, 64, q0, hq, pol);
+            }
+            uint64_t* freed = which ? bar_vfree : bar_kfree;
             int2 ids[kPagesPerTile], nxt[kPagesPerTile];
             if (n_tiles > 0) load_ids(0, ids);
             for (int j = 0; j < n_tiles && ok; ++j) {
-                const int st = j & 1;
                 if (j + 1 < n_tiles) load_ids(j + 1, nxt);
-                if (j >= 2) wait(&bar_s[st], ((j - 2) >> 1) & 1);
+                if (which == 0) { PROBE_LD(0); }
+                if (j >= kStages) wait(&freed[j % kStages], (j / kStages - 1) & 1);
+                if (which == 0) { PROBE_LD(1); }
                 if (!ok) break;
-                issue(j, 0, ids);
-                if (j >= 2) wait(&bar_vfree[st], ((j - 2) >> 1) & 1);
-                if (!ok) break;
-                issue(j, 1, ids);
+                issue(j, which, ids);
+                if (which == 0) { PROBE_LD(2); }
 #pragma unroll
                 for (int i = 0; i < kPagesPerTile; ++i) ids[i] = nxt[i];
             }
-            if (n_tiles == 0) wait(bar_q, 0);  // the Q load must land before the CTA exits
+            if (which == 0 && n_tiles == 0) wait(bar_q, 0);  // the Q load must land before the CTA exits
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
@@ -271,68 +371,135 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
     const int r = tid & 127;  // query row of this thread
     const int hc = tid >> 7;  // which 64 of the 128 key columns (and O columns)
-    const uint32_t t_x = tmem + lane_base + 384;  // exchange columns: [384 + 2 hc, +2)
+    const uint32_t t_x = tmem + lane_base + kColX;  // exchange columns: [kColX + 2 hc, +2)
+    if (n_tiles > 0) {
+        // Q into TMEM: this thread's row r, dims [64 hc, +64) from the
+        // swizzled smem tile, two dims per column (lower dim in the low half).
+        wait(bar_q, 0);
+        uint32_t qw[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(smem + kOffQ + hc * kHalf + r * 128 + ((c ^ (r & 7)) << 4));
+            qw[4 * c] = v.x;
+            qw[4 * c + 1] = v.y;
+            qw[4 * c + 2] = v.z;
+            qw[4 * c + 3] = v.w;
+        }
+        tc::st32(tmem + lane_base + kColQ + hc * 32, *reinterpret_cast<const float(*)[32]>(qw));
+        tc::wait_st();
+        tc::fence_before_sync();
+        consumer_sync();
+        if (tid == 0) mbar_arrive(bar_qt);
+    }
     const int q_abs = first_q_abs + r;
     const int lim = a.causal ? min(q_abs, a.total - 1) : a.total - 1;  // last visible key
     float m_run = -INFINITY, l_run = 0.f;
+    // Lanes 0-7 of every consumer warp hold the next tile's page entries
+    // (fetched a tile ahead) to derive its copy mode.
+    const int lane = tid & 31;
+    auto entry = [&](int j) {
+        int lp = (j0 + j) * kPagesPerTile + (lane & (kPagesPerTile - 1));
+        if (lp >= a.n_pages) lp = a.n_pages - 1;
+        return a.table[lp];
+    };
+    int2 next_e = n_tiles > 0 ? entry(0) : make_int2(0, 0);
+
+    // S(j) is loaded from TMEM at the end of tile j-1, so the load latency
+    // overlaps the loop turn-around.
+    float s[64];
+    auto load_s = [&](int j) {
+        wait(&bar_s[j & 1], (j >> 1) & 1);
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+            tc::ld32(tmem + lane_base + (j & 1) * 128 + hc * 64 + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+    };
+    if (n_tiles > 0) load_s(0);
 
     for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
+        const int2 cur_e = next_e;  // page entries of tile j (lanes 0-7)
+        if (j + 1 < n_tiles) next_e = entry(j + 1);
         PROBE_PF(0);
-        wait(&bar_s[st], (j >> 1) & 1);
-        PROBE_PF(1);
-        tc::fence_after_sync();
         const int key0 = (j0 + j) * kBN;
+        tc::wait_ld_into(*reinterpret_cast<float(*)[32]>(&s[0]));
+        tc::reg_dep(*reinterpret_cast<float(*)[32]>(&s[32]));
+        PROBE_PF(1);
 
-        float s[64];
+        // Row max over the tile: local over this thread's 64 keys, then one
+        // exchange with the row's other thread through spare TMEM columns.
+        // Scores stay unscaled here (qscale > 0 keeps the order).
+        const int n_ok = max(0, min(kBN, lim - key0 + 1));  // keys [0, n_ok) of the tile are visible
+        if (!__all_sync(0xFFFFFFFFu, n_ok >= kBN)) {
+            const int mode = tile_mode_warp(cur_e, lane, a.pool_pages, a.runs);
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-            tc::ld32(tmem + lane_base + st * 128 + hc * 64 + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
-        tc::wait_ld();
-
-        // Local max and sum over this thread's 64 columns, one exchange with
-        // the row's other thread, then a common max.
-        const int n_ok = max(0, min(kBN, lim - key0 + 1)) - hc * 64;
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            const float v = c < n_ok ? s[c] * a.qscale : -INFINITY;
-            s[c] = v;
-            mx = fmaxf(mx, v);
+            for (int c = 0; c < 64; ++c)
+                if (tile_key(hc * 64 + c, mode) >= n_ok) s[c] = -INFINITY;
         }
-        const float ml_use = mx == -INFINITY ? 0.f : mx;
-        float sum = 0.f;
+        float mx = s[0];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            const float p = exp2_approx(s[c] - ml_use);
-            s[c] = p;
-            sum += p;
-        }
+        for (int c = 1; c < 64; ++c) mx = fmaxf(mx, s[c]);
         PROBE_PF(2);
-        tc::st2(t_x + 2 * hc, mx, sum);
+        tc::st2(t_x + 2 * hc, mx, 0.f);
         tc::wait_st();
         tc::fence_before_sync();
         consumer_sync();
         tc::fence_after_sync();
         PROBE_PF(3);
-        float mx2, sum2;
-        tc::ld2(t_x + 2 * (1 - hc), mx2, sum2);
+        float mx2, unused;
+        tc::ld2(t_x + 2 * (1 - hc), mx2, unused);
         tc::wait_ld();
-        const float m_new = fmaxf(m_run, fmaxf(mx, mx2));
+        // Lazy rescaling: the reference max m_run moves only when the tile's
+        // max exceeds it by more than kRescaleLog2 (P then stays <= 2^8, exact
+        // in the fp32 accumulators and the hi/lo split); O and l are rescaled
+        // only then, so most tiles never wait for the previous P V.
+        const float m_tile = fmaxf(mx, mx2) * a.qscale;
+        const bool move = m_tile > m_run + kRescaleLog2;
+        const float m_new = move ? m_tile : m_run;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = exp2_approx(m_run - m_use);
-        const float f_me = exp2_approx(mx - m_use), f_other = exp2_approx(mx2 - m_use);
+        const float alpha = move ? exp2_approx(m_run - m_use) : 1.f;
+        // P = 2^(s * qscale - m), split into bf16 hi + bf16 lo, both by
+        // truncation (the upper 16 bits; no conversion instructions): hi holds
+        // P to 2^-7 relative, lo = P - hi (exact in fp32) to 2^-7 of itself,
+        // so hi + lo carries P to 2^-14, where a single bf16 P would lose 2^-9
+        // per probability. Packed two keys per 32-bit word, lower key in the
+        // low half, as the MMA reads A from TMEM. Four partial sums keep the
+        // dependent FADD chain short.
+        // Two passes of 32 keys; each pass's stores to TMEM run while the
+        // next pass computes.
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        const float neg_m = -m_use;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) s[c] *= f_me;
-        l_run = l_run * alpha + sum * f_me + sum2 * f_other;
+        for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t hw[16], lw[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float p0 = exp2_approx(fmaf(s[h2 * 32 + 2 * i], a.qscale, neg_m));
+                const float p1 = exp2_approx(fmaf(s[h2 * 32 + 2 * i + 1], a.qscale, neg_m));
+                sum4[i & 3] += p0 + p1;
+                const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+                hw[i] = __byte_perm(b0, b1, 0x7632);
+                const float r0 = p0 - __uint_as_float(b0 & 0xFFFF0000u), r1 = p1 - __uint_as_float(b1 & 0xFFFF0000u);
+                lw[i] = __byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632);
+            }
+            // P(j) overwrites S(j) in TMEM: hi in the buffer's columns
+            // [0, 64), lo in [64, 128); this thread's 64 keys are 32 columns
+            // of each.
+            tc::st16(tmem + lane_base + st * 128 + hc * 32 + h2 * 16, hw);
+            tc::st16(tmem + lane_base + st * 128 + 64 + hc * 32 + h2 * 16, lw);
+        }
+        const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+        PROBE_PF(4);
+        l_run = l_run * alpha + sum;  // this thread's share of the row sum
         m_run = m_new;
 
-        if (j > 0) {
-            // P V of tile j-1 must be done before P and O are touched.
-            wait(bar_o, (j - 1) & 1);
-            PROBE_PF(4);
+        if (j > 0 && __any_sync(0xFFFFFFFFu, move)) {
+            // P V of tile j-1 must be done before O is rescaled. (The stage's
+            // previous P V is done already: V(j-1) was loaded into the stage
+            // after it, so the barrier's parity identifies PV(j-1).)
+            wait(&bar_vfree[(j - 1) % kStages], ((j - 1) / kStages) & 1);
             tc::fence_after_sync();
-            if (__any_sync(0xFFFFFFFFu, alpha != 1.f)) {
+            {
 #pragma unroll
                 for (int c = hc * 2; c < hc * 2 + 2; ++c) {
                     float o[32];
@@ -342,47 +509,31 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     for (int i = 0; i < 32; ++i) o[i] *= alpha;
                     tc::st32(t_o + c * 32, o);
                 }
-                tc::wait_st();
             }
         }
-
-        // P into the swizzled K-major layout (row r, 16-byte chunk c of each
-        // 64-key half at position c ^ (r & 7)) as two bf16 terms, hi = bf16(P)
-        // and lo = bf16(P - hi): P.V = hi.V + lo.V keeps fp32-level accuracy
-        // where a single bf16 P would lose 2^-9 relative per probability.
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-            const int c = hc * 8 + c8;
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float x0 = s[c8 * 8 + 2 * i], x1 = s[c8 * 8 + 2 * i + 1];
-                const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-                const float2 hf2 = __bfloat1622float2(h2);
-                const __nv_bfloat162 l2 = __floats2bfloat162_rn(x0 - hf2.x, x1 - hf2.y);
-                hw[i] = *reinterpret_cast<const uint32_t*>(&h2);
-                lw[i] = *reinterpret_cast<const uint32_t*>(&l2);
-            }
-            const int hf = c >> 3, cc = c & 7;
-            const uint32_t off = hf * kHalf + r * 128 + ((cc ^ (r & 7)) * 16);
-            *reinterpret_cast<uint4*>(smem + kOffP + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(smem + kOffPlo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
+        tc::wait_st();
         PROBE_PF(5);
-        // V(j) must have landed; zero its rows past the cache.
-        wait(&bar_v[st], (j >> 1) & 1);
+        // V(j) must have landed; zero its rows past the cache (P is 0 there,
+        // but stale rows could hold NaN or Inf).
+        const int vst = j % kStages;
+        wait(&bar_v[vst], (j / kStages) & 1);
         PROBE_PF(6);
         const int valid_rows = min(kBN, a.total - key0);
-        if (r >= valid_rows) {
-            uint4* v0 = reinterpret_cast<uint4*>(smem + kOffV + st * kTile + hc * kHalf + r * 128);
+        if (valid_rows < kBN) {  // CTA-uniform
+            const int mode = tile_mode_warp(cur_e, lane, a.pool_pages, a.runs);
+            if (tile_key(r, mode) >= valid_rows) {
+                uint4* v0 = reinterpret_cast<uint4*>(smem + kOffV + vst * kTile + hc * kHalf + r * 128);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) v0[c] = make_uint4(0, 0, 0, 0);
+                for (int c = 0; c < 8; ++c) v0[c] = make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();
         }
-        fence_proxy_async_smem();
         tc::fence_before_sync();
         consumer_sync();
         PROBE_PF(7);
         if (tid == 0) mbar_arrive(bar_p);
+        PROBE_PF(8);
+        if (j + 1 < n_tiles) load_s(j + 1);
     }
 
     if (n_tiles > 0) wait(bar_o, (n_tiles - 1) & 1);
@@ -394,6 +545,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     if (n_tiles == 0) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    }
+    {
+        // Each thread holds the sum over its own 64 keys of every tile.
+        tc::st2(t_x + 2 * hc, l_run, 0.f);
+        tc::wait_st();
+        tc::fence_before_sync();
+        consumer_sync();
+        tc::fence_after_sync();
+        float l2, unused;
+        tc::ld2(t_x + 2 * (1 - hc), l2, unused);
+        tc::wait_ld();
+        l_run += l2;
     }
     float l_fin = l_run;
     if (n_split > 1) {
@@ -470,9 +633,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
 }  // namespace
 
-cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const CUtensorMap& k_map,
-                              const CUtensorMap& v_map, const int2* table, const PrefillLaunch& p, uint32_t* err,
-                              int num_sms, cudaStream_t stream) {
+cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const PoolMaps& maps,
+                              const int2* table, const PrefillLaunch& p, uint32_t* err, int num_sms,
+                              cudaStream_t stream) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -494,6 +657,7 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
     a.n_pages = p.n_pages;
     a.pool_pages = pool.pool_pages;
     a.causal = p.causal;
+    a.runs = maps.runs ? 1 : 0;
     a.qscale = p.scale * 1.4426950408889634f;
     // Split the KV range over a cluster of up to 3 CTAs while the query tiles
     // alone would leave SMs idle.
@@ -513,7 +677,7 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
     attr[0].val.clusterDim.z = n_split;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, k_map, v_map, a);
+    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, maps.k, maps.v, maps.k_run, maps.v_run, a);
 }
 
 }  // namespace gkv
@@ -521,5 +685,11 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
 #ifdef GKV_PROBE_TIMELINE
 extern "C" int gkv_probe_read_prefill(long long* out, int n) {
     return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_pf, sizeof(long long) * n);
+}
+extern "C" int gkv_probe_read_prefill_ld(long long* out, int n) {
+    return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_ld, sizeof(long long) * n);
+}
+extern "C" int gkv_probe_read_prefill_mma(long long* out, int n) {
+    return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_mma, sizeof(long long) * n);
 }
 #endif

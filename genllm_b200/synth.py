@@ -79,12 +79,19 @@ class FragmentedCase:
 
 def fragmented_case(seed: int, n_q_heads: int, n_kv_heads: int, head_dim: int, n_prior: int,
                     pool_pages: int, n_new: int = 1, fill_pools: bool = True,
-                    poison_unused: bool = False) -> FragmentedCase:
+                    poison_unused: bool = False, page_order: str = "random") -> FragmentedCase:
     """Build the inputs of one paged-attention step.
 
     Config 1 of the path (Qwen3-0.6B layer): ``fragmented_case(0, 16, 8, 128,
     1024, 256)``. With ``poison_unused`` the slots no table entry covers hold
     NaN bit patterns, so a kernel that reads past the valid tokens shows up.
+
+    ``page_order`` sets the physical ids behind the logical pages: "random"
+    (a shuffled pool), "asc" (0, 1, 2, ...), "desc" (the highest ids first,
+    as the LIFO free list hands them out after a reset; the step's new pages
+    then come back ascending), "broken" (descending with some runs of 8
+    interrupted: two ids swapped in one run, V alone swapped in another) and
+    "kv_mismatch" (K descending, V ascending).
     """
     rng = np.random.default_rng(seed)
     n_pages = (n_prior + PAGE_SLOTS - 1) // PAGE_SLOTS
@@ -92,6 +99,22 @@ def fragmented_case(seed: int, n_q_heads: int, n_kv_heads: int, head_dim: int, n
         raise ValueError("pool too small for the prior tokens")
     kp = rng.permutation(pool_pages).astype(np.int32)
     vp = rng.permutation(pool_pages).astype(np.int32)
+    if page_order != "random":
+        up = np.arange(pool_pages, dtype=np.int32)
+        if page_order == "asc":
+            kp, vp = up.copy(), up.copy()
+        elif page_order in ("desc", "broken"):
+            kp, vp = up[::-1].copy(), up[::-1].copy()
+            if page_order == "broken":
+                if pool_pages > 12:
+                    kp[[11, 12]] = kp[[12, 11]]
+                    vp[[11, 12]] = vp[[12, 11]]
+                if pool_pages > 20:
+                    vp[[19, 20]] = vp[[20, 19]]
+        elif page_order == "kv_mismatch":
+            kp, vp = up[::-1].copy(), up.copy()
+        else:
+            raise ValueError(f"unknown page_order {page_order!r}")
     shape = (pool_pages, PAGE_SLOTS, n_kv_heads, head_dim)
     if fill_pools:
         k_pool = randn_bf16(rng, shape)

@@ -327,3 +327,16 @@ def test_prefill_tile_edges(n_prior, n_new, causal):
     case = fragmented_case(500 + n_new, 16, 8, 128, n_prior, (n_prior + n_new) // 16 + 3, n_new=n_new,
                            poison_unused=True)
     check_case(case, causal)
+
+
+@pytest.mark.parametrize("order", ["asc", "desc", "broken", "kv_mismatch"])
+@pytest.mark.parametrize("n_prior,n_new,causal", [(1000, 300, True), (2040, 130, True), (517, 256, False)])
+def test_prefill_page_runs(order, n_prior, n_new, causal):
+    """Tiles whose 8 pages have consecutive ids are copied as one run
+    (ascending, or descending and reversed in shared memory); interrupted
+    runs and K/V tables that disagree fall back to page-by-page copies.
+    Contexts ending mid-page and causal diagonals cross reversed tiles."""
+    case = fragmented_case(600 + n_new, 16, 8, 128, n_prior, (n_prior + n_new) // 16 + 24, n_new=n_new,
+                           poison_unused=True, page_order=order)
+    check_case(case, causal)
+
