@@ -139,3 +139,45 @@ def fragmented_case(seed: int, n_q_heads: int, n_kv_heads: int, head_dim: int, n
                           kp[:n_pages].copy(), vp[:n_pages].copy(), kp[n_pages:].copy(),
                           vp[n_pages:].copy(), k_pool, v_pool, q, k_new, v_new,
                           float(1.0 / np.sqrt(head_dim)))
+
+
+@dataclass
+class QkRopeCase:
+    """Inputs of the QK-norm + RoPE step that feeds the attention op, as the
+    reference's Qwen3 block produces them (src/model/Qwen3.cpp:130-154):
+    q_flat [S][Hq*D] and k_flat / v_flat [S][Hkv*D] bf16 (the projections'
+    outputs), per-head RMSNorm weights [D] fp32, eps, RoPE theta and the
+    position of the first token."""
+    q_flat: np.ndarray
+    k_flat: np.ndarray
+    v_flat: np.ndarray
+    q_norm_w: np.ndarray
+    k_norm_w: np.ndarray
+    eps: float
+    theta: float
+    start_pos: int
+    n_q_heads: int
+    n_kv_heads: int
+    head_dim: int
+
+    @property
+    def seq_len(self) -> int:
+        return self.q_flat.shape[0]
+
+
+def qk_rope_case(seed: int, n_q_heads: int, n_kv_heads: int, seq_len: int, start_pos: int,
+                 head_dim: int = 128, eps: float = 1e-6, theta: float = 1e6) -> QkRopeCase:
+    rng = np.random.default_rng(seed)
+    q = randn_bf16(rng, (seq_len, n_q_heads * head_dim))
+    k = randn_bf16(rng, (seq_len, n_kv_heads * head_dim))
+    v = randn_bf16(rng, (seq_len, n_kv_heads * head_dim))
+    wq = (1.0 + 0.25 * rng.standard_normal(head_dim)).astype(np.float32)
+    wk = (1.0 + 0.25 * rng.standard_normal(head_dim)).astype(np.float32)
+    return QkRopeCase(q, k, v, wq, wk, eps, theta, start_pos, n_q_heads, n_kv_heads, head_dim)
+
+
+def heads_major(flat: np.ndarray, n_heads: int) -> np.ndarray:
+    """[S][H*D] -> [H][S][D]: the reference's reshape_permute {0, 2, 1, 3}."""
+    S = flat.shape[0]
+    return np.ascontiguousarray(flat.reshape(S, n_heads, -1).transpose(1, 0, 2))
+

@@ -76,6 +76,12 @@ class Oracle:
         L.orc_bf16_from_f32.argtypes = [C.c_float]
         L.orc_bf16_from_f32.restype = C.c_uint16
         L.orc_round_bf16.argtypes = [_vp, _vp, C.c_size_t]
+        L.orc_rms_norm_bf16.argtypes = [_vp, _vp, _vp, C.c_int64, C.c_int64, C.c_float]
+        L.orc_rms_norm_bf16.restype = None
+        L.orc_apply_rope_bf16.argtypes = [_vp, _vp, _vp, _vp] + [C.c_int64] * 4
+        L.orc_apply_rope_bf16.restype = None
+        L.orc_rope_cache.argtypes = [C.c_float, C.c_int32, C.c_int32, _vp, _vp]
+        L.orc_rope_cache.restype = None
 
     def paged_attention_f32(self, q, k_pool, v_pool, k_ids, v_ids, total, n_q_heads, n_kv_heads,
                             seq_len, head_dim, scale, causal=True, dtype=BF16, threads=0):
@@ -113,6 +119,30 @@ class Oracle:
         out = np.empty(x.shape, dtype=np.uint16)
         self.lib.orc_round_bf16(_ptr(x), _ptr(out), x.size)
         return out
+
+    def rms_norm_bf16(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        """Rows of x (uint16 bf16, last axis = len(w)) normalised: qk_rope_oracle.c."""
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        out = np.empty_like(x)
+        self.lib.orc_rms_norm_bf16(_ptr(x), _ptr(w), _ptr(out), x.size // w.size, w.size, eps)
+        return out
+
+    def apply_rope_bf16(self, x: np.ndarray, cos: np.ndarray, sin: np.ndarray, start_pos: int) -> np.ndarray:
+        """x: uint16 [H][S][D]; cos/sin f32 [max_seq][D]."""
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        cos = np.ascontiguousarray(cos, dtype=np.float32)
+        sin = np.ascontiguousarray(sin, dtype=np.float32)
+        out = np.empty_like(x)
+        H, S, D = x.shape
+        self.lib.orc_apply_rope_bf16(_ptr(x), _ptr(out), _ptr(cos), _ptr(sin), H, S, D, start_pos)
+        return out
+
+    def rope_cache(self, theta: float, head_dim: int, max_seq: int):
+        cos = np.empty((max_seq, head_dim), dtype=np.float32)
+        sin = np.empty((max_seq, head_dim), dtype=np.float32)
+        self.lib.orc_rope_cache(theta, head_dim, max_seq, _ptr(cos), _ptr(sin))
+        return cos, sin
 
 
 class OraclePool:
@@ -202,6 +232,51 @@ class OraclePool:
 
 def ref_available() -> bool:
     return os.path.exists(REF_SO)
+
+
+REF_OPS_SO = os.path.join(HERE, "_ref", "libgenllm_ref_ops.so")
+
+
+def ref_ops_available() -> bool:
+    return os.path.exists(REF_OPS_SO)
+
+
+class RefOps:
+    """The reference's own CPU RMSNorm / RoPE / RoPE-cache ops
+    (oracle/_ref/libgenllm_ref_ops.so, built with the reference's CPU flags)."""
+
+    def __init__(self, path: str = REF_OPS_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref` where the reference tree exists")
+        L = self.lib = C.CDLL(path)
+        L.ref_rms_norm.argtypes = [_vp, _vp, _vp, C.c_int64, C.c_int64, C.c_float]
+        L.ref_rms_norm.restype = None
+        L.ref_apply_rope.argtypes = [_vp, _vp, _vp, _vp] + [C.c_int64] * 5
+        L.ref_apply_rope.restype = None
+        L.ref_rope_cache.argtypes = [C.c_float, C.c_int32, C.c_int32, _vp, _vp]
+        L.ref_rope_cache.restype = None
+
+    def rms_norm_bf16(self, x, w, eps):
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        out = np.empty_like(x)
+        self.lib.ref_rms_norm(_ptr(x), _ptr(w), _ptr(out), x.size // w.size, w.size, eps)
+        return out
+
+    def apply_rope_bf16(self, x, cos, sin, start_pos):
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        cos = np.ascontiguousarray(cos, dtype=np.float32)
+        sin = np.ascontiguousarray(sin, dtype=np.float32)
+        out = np.empty_like(x)
+        H, S, D = x.shape
+        self.lib.ref_apply_rope(_ptr(x), _ptr(out), _ptr(cos), _ptr(sin), H, S, D, start_pos, cos.shape[0])
+        return out
+
+    def rope_cache(self, theta, head_dim, max_seq):
+        cos = np.empty((max_seq, head_dim), dtype=np.float32)
+        sin = np.empty((max_seq, head_dim), dtype=np.float32)
+        self.lib.ref_rope_cache(theta, head_dim, max_seq, _ptr(cos), _ptr(sin))
+        return cos, sin
 
 
 class RefSession:

@@ -104,6 +104,12 @@ void orc_paged_attention_rows(const uint8_t* q, int32_t dtype, const uint8_t* k_
                               int32_t head_dim, int32_t n_kv_groups, float scale, int causal,
                               const int32_t* rows, int32_t n_rows, float* out, int32_t n_threads);
 
+/* qk_rope_oracle.c: per-head RMSNorm (QK-norm) and RoPE, bf16 in and out. */
+void orc_rms_norm_bf16(const uint16_t* x, const float* w, uint16_t* out, int64_t rows, int64_t dim, float eps);
+void orc_apply_rope_bf16(const uint16_t* x, uint16_t* out, const float* cos_tab, const float* sin_tab,
+                         int64_t n_heads, int64_t seq, int64_t head_dim, int64_t start_pos);
+void orc_rope_cache(float theta, int32_t head_dim, int32_t max_seq, float* cos_out, float* sin_out);
+
 /* Round an fp32 buffer to the reference's bf16 (RNE, subnormals to signed 0). */
 void orc_round_bf16(const float* in, uint16_t* out, size_t n);
 

@@ -17,3 +17,14 @@ SMALL = [
 ]
 
 CONFIG1 = ("config1", dict(seed=0, n_q_heads=16, n_kv_heads=8, head_dim=128, n_prior=1024, pool_pages=256), True)
+
+# QK-norm + RoPE (the step that produces the K the attention op appends):
+# (name, qk_rope_case kwargs, max_seq of the RoPE table). The fixtures hold the
+# reference's normalised + rotated Q and K ([H][S][D] bf16) and a checksum of
+# its cos/sin table.
+QK_ROPE = [
+    ("qkrope_chunk", dict(seed=31, n_q_heads=16, n_kv_heads=8, seq_len=7, start_pos=1000), 4096),
+    ("qkrope_decode_32k", dict(seed=32, n_q_heads=32, n_kv_heads=8, seq_len=1, start_pos=32768), 40960),
+    ("qkrope_from_zero", dict(seed=33, n_q_heads=4, n_kv_heads=2, seq_len=20, start_pos=0), 64),
+]
+

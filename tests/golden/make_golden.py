@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory from the REFERENCE itself.
 
-Runs the unmodified reference CPU op (oracle/_ref/libgenllm_ref.so, compiled
-from the Genllm sources by oracle/Makefile) on the seeded cases of cases.py
-and stores its outputs. Needs the reference tree (only present where the
+Runs the unmodified reference CPU ops (oracle/_ref/libgenllm_ref.so and
+libgenllm_ref_ops.so, compiled from the Genllm sources by oracle/Makefile) on
+the seeded cases of cases.py and stores their outputs. Needs the reference tree (only present where the
 fixtures are made); the tests only read the .npz files.
 
     make -C oracle && python tests/golden/make_golden.py
@@ -18,9 +18,9 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, HERE)
 
-from cases import CONFIG1, SMALL  # noqa: E402
-from genllm_b200.synth import fragmented_case  # noqa: E402
-from oracle.oracle import run_ref_case  # noqa: E402
+from cases import CONFIG1, QK_ROPE, SMALL  # noqa: E402
+from genllm_b200.synth import fragmented_case, heads_major, qk_rope_case  # noqa: E402
+from oracle.oracle import RefOps, run_ref_case  # noqa: E402
 
 
 def sha(a: np.ndarray) -> str:
@@ -45,6 +45,26 @@ def main():
                                                             sha(c.k_new), sha(c.v_new)]),
                         pools_after_sha=np.array([sha(kp), sha(vp)]))
     print(name, out.shape, nc)
+    make_qk_rope()
+
+
+def make_qk_rope():
+    """Reference pipeline of src/model/Qwen3.cpp:136-154: reshape_permute to
+    [H][S][D], per-head rms_norm, apply_rope at start_pos."""
+    R = RefOps()
+    for name, kw, max_seq in QK_ROPE:
+        c = qk_rope_case(**kw)
+        cos, sin = R.rope_cache(c.theta, c.head_dim, max_seq)
+        q4 = heads_major(c.q_flat, c.n_q_heads)
+        k4 = heads_major(c.k_flat, c.n_kv_heads)
+        qn = R.rms_norm_bf16(q4, c.q_norm_w, c.eps)
+        kn = R.rms_norm_bf16(k4, c.k_norm_w, c.eps)
+        qr = R.apply_rope_bf16(qn, cos, sin, c.start_pos)
+        kr = R.apply_rope_bf16(kn, cos, sin, c.start_pos)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), q_rope=qr, k_rope=kr, q_normed=qn, k_normed=kn,
+                            cache_sha=np.array([sha(cos), sha(sin)]),
+                            inputs_sha=np.array([sha(c.q_flat), sha(c.k_flat), sha(c.q_norm_w), sha(c.k_norm_w)]))
+        print(name, qr.shape, kr.shape)
 
 
 if __name__ == "__main__":
