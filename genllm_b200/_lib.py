@@ -45,6 +45,11 @@ class NewPages(C.Structure):
     _fields_ = [("first_new_page", i32), ("n_new_pages", i32), ("k_ids", i32p), ("v_ids", i32p)]
 
 
+class QkNormDesc(C.Structure):
+    _fields_ = [("q_norm_w", vp), ("k_norm_w", vp), ("cos_tab", vp), ("sin_tab", vp), ("max_seq", i32),
+                ("eps", C.c_float)]
+
+
 # name -> (argtypes, restype); every entry point returns an int status unless noted.
 SIGNATURES = {
     "gkv_status_string": ([C.c_int], C.c_char_p),
@@ -86,6 +91,12 @@ SIGNATURES = {
     "gkv_paged_attention_gather": ([vp, i32, vp, vp, vp, vp, C.c_size_t, i32, C.c_float, i32, vp], C.c_int),
     "gkv_paged_decode_static_scratch": ([C.POINTER(PoolDesc), vp, i32, vp, vp, vp, vp, i32, C.c_float, i32, vp],
                                         C.c_int),
+    "gkv_rope_cache": ([C.c_float, i32, i32, vp, vp], C.c_int),
+    "gkv_qk_norm_rope": ([vp, vp, vp, i32, i32, i32, C.POINTER(QkNormDesc), i32, vp, vp, vp, vp], C.c_int),
+    "gkv_paged_attention_raw_qknorm": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), vp, vp, vp, vp, i32, i32,
+                                        C.c_float, i32, i32, C.POINTER(QkNormDesc), vp], C.c_int),
+    "gkv_paged_attention_qknorm": ([vp, i32, vp, vp, vp, vp, i32, i32, C.c_float, i32, i32, C.POINTER(QkNormDesc),
+                                    vp], C.c_int),
 }
 
 

@@ -33,6 +33,7 @@
 
 #include "device.cuh"
 #include "kernels.h"
+#include "qk_rope.cuh"
 
 namespace gkv {
 namespace {
@@ -75,6 +76,8 @@ struct DecodeParams {
     int32_t pages_per_stage;  // P = 8 / Hkv (floored)
     int32_t new_first;
     int32_t new_n;
+    int32_t qk_on;  // 1: q / k_new are pre-norm projections: QK-norm + RoPE here (position n_prior)
+    QkNorm qk;
     float qscale;  // softmax scale * log2(e)
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
@@ -228,7 +231,38 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("griddepcontrol.wait;" ::: "memory");
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
         uint32_t qb[8][2];
-        {
+        if (a.qk_on) {
+            // QK-norm + RoPE of this warp's G query rows, each through a
+            // 256-byte staging row (the warp's P buffer, idle until the first
+            // page) from which each lane takes its fragment.
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) qb[kk][0] = qb[kk][1] = 0u;
+            if (active) {
+                float xq[8][4];
+#pragma unroll
+                for (int n = 0; n < 8; ++n)
+                    if (n < G) load_row4(a.q + (size_t)(head * G + n) * kHeadDim, lane, xq[n]);
+                const size_t pos = (size_t)a.n_prior * kHeadDim;
+                uint16_t* stage = reinterpret_cast<uint16_t*>(pbuf);
+#pragma unroll
+                for (int n = 0; n < 8; ++n) {
+                    if (n >= G) break;
+                    uint16_t o[4];
+                    norm_rope_row(xq[n], lane, a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, a.qk.eps, o);
+#pragma unroll
+                    for (int it = 0; it < 4; ++it) stage[lane + 32 * it] = o[it];
+                    __syncwarp();
+                    if (g == n) {
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            qb[kk][0] = *reinterpret_cast<const uint32_t*>(stage + kk * 16 + 2 * t);
+                            qb[kk][1] = *reinterpret_cast<const uint32_t*>(stage + kk * 16 + 2 * t + 8);
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+        } else {
             const int n = g;
             const bool valid = active && n < G;
             const uint16_t* qr = a.q + (size_t)(head * G + (valid ? n : 0)) * kHeadDim;
@@ -269,7 +303,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                 // Fused append of this step's token.
                 if (a.k_new != nullptr && a.n_prior >= base && a.n_prior < base + kPageSlots) {
                     const int slot = a.n_prior - base;
-                    const uint2 kk = *reinterpret_cast<const uint2*>(a.k_new + (size_t)head * kHeadDim + lane * 4);
+                    uint2 kk;
+                    if (a.qk_on) {  // the post-QK-norm, post-RoPE row is what the page holds
+                        float xk[4];
+                        load_row4(a.k_new + (size_t)head * kHeadDim, lane, xk);
+                        const size_t pos = (size_t)a.n_prior * kHeadDim;
+                        uint16_t o[4];
+                        norm_rope_row(xk, lane, a.qk.k_w, a.qk.cos + pos, a.qk.sin + pos, a.qk.eps, o);
+                        uint16_t* stage = reinterpret_cast<uint16_t*>(pbuf);
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) stage[lane + 32 * it] = o[it];
+                        __syncwarp();
+                        kk = *reinterpret_cast<const uint2*>(stage + lane * 4);
+                        __syncwarp();
+                    } else {
+                        kk = *reinterpret_cast<const uint2*>(a.k_new + (size_t)head * kHeadDim + lane * 4);
+                    }
                     const uint2 vv = *reinterpret_cast<const uint2*>(a.v_new + (size_t)head * kHeadDim + lane * 4);
                     const uint32_t o = tile_off(slot, lane >> 1) + (lane & 1) * 8;
                     *reinterpret_cast<uint2*>(kt + o) = kk;
@@ -631,6 +680,8 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     p.qscale = d.scale * 1.4426950408889634f;
     p.new_first = np.first;
     p.new_n = np.n;
+    p.qk_on = d.qk ? 1 : 0;
+    if (d.qk) p.qk = *d.qk;
 #ifdef GKV_PROBE_TIMELINE
     static int probe_counter = 0;
     p.probe_slot = probe_counter++ % 8;

@@ -20,6 +20,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <climits>
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -169,6 +170,8 @@ struct gkv_table {
     CUtensorMap k_map_run;  // box {64 dims, 1 head, 128 slots}: 8 pages with consecutive ids
     CUtensorMap v_map_run;
     bool runs = false;      // run maps valid (the pool holds at least 8 pages)
+    void* qk_buf = nullptr;  // normalised / rotated / permuted Q, K, V of a chunk (gkv_paged_attention_raw_qknorm)
+    size_t qk_bytes = 0;
 };
 
 namespace {
@@ -178,6 +181,7 @@ void table_free(gkv_table* t) {
     cudaFree(t->scratch.part_acc);
     cudaFree(t->scratch.part_ml);
     cudaFree(t->scratch.err);
+    cudaFree(t->qk_buf);
 }
 
 constexpr int kMaxKvHeads = 256;
@@ -367,10 +371,35 @@ int gkv_append_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, 
     return append_chunks(pool, t, n_prior, np, K, V, seq_len, reinterpret_cast<cudaStream_t>(stream));
 }
 
+namespace {
+int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np, const void* Q,
+                  const void* K, const void* V, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
+                  int32_t causal, int32_t out_dtype, const gkv::QkNorm* qk, gkv_stream_t stream);
+}  // namespace
+
 int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
                             const void* Q, const void* K, const void* V, void* out, int32_t n_q_heads,
                             int32_t seq_len, float scale, int32_t causal, int32_t out_dtype,
                             gkv_stream_t stream) {
+    return attention_raw(pool, t, n_prior, np, Q, K, V, out, n_q_heads, seq_len, scale, causal, out_dtype, nullptr,
+                         stream);
+}
+
+namespace {
+// Validate a gkv_qk_norm for positions [start, start + seq_len).
+int check_qk(const gkv_qk_norm* qk, int32_t start, int32_t seq_len) {
+    if (!qk || !qk->q_norm_w || !qk->k_norm_w || !qk->cos_tab || !qk->sin_tab)
+        return fail(GKV_ERR_INVALID, "gkv_qk_norm: null weight or table");
+    if (start < 0 || (int64_t)start + seq_len > qk->max_seq)
+        return fail(GKV_ERR_INVALID, "positions [%d, %d) exceed the RoPE table (%d rows)", start, start + seq_len,
+                    qk->max_seq);
+    if (!(qk->eps >= 0.f)) return fail(GKV_ERR_INVALID, "eps %g", (double)qk->eps);
+    return GKV_OK;
+}
+
+int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np, const void* Q,
+                  const void* K, const void* V, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
+                  int32_t causal, int32_t out_dtype, const gkv::QkNorm* qk, gkv_stream_t stream) {
     int st = check_pool(pool);
     if (st) return st;
     if (!t || n_prior < 0 || seq_len < 1 || !Q || !K || !V || !out)
@@ -415,6 +444,7 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
         d.n_pages = n_pages;
         d.scale = scale;
         d.n_splits = 0;
+        d.qk = qk;
         cudaError_t e =
             gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s, t_gather);
         if (e != cudaSuccess) return cuda_fail(e, "decode launch");
@@ -445,6 +475,85 @@ int gkv_paged_attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_p
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
     return GKV_OK;
+}
+}  // namespace
+
+int gkv_rope_cache(float theta, int32_t head_dim, int32_t max_seq, float* cos_out, float* sin_out) {
+    if (head_dim < 2 || head_dim % 2 || max_seq < 0 || !cos_out || !sin_out || !(theta > 0.f))
+        return fail(GKV_ERR_INVALID, "gkv_rope_cache: bad arguments");
+    // RopeCacheImpl<CPU> (src/backend/cpu/rope.cpp:112-140): angles in double,
+    // inv_freq_i = theta^(-2i/d); cos/sin rounded to float, written to
+    // columns i and i + d/2.
+    const int32_t half = head_dim / 2;
+    std::vector<double> inv(half);
+    for (int32_t i = 0; i < half; ++i)
+        inv[i] = 1.0 / std::pow(static_cast<double>(theta), (2.0 * i) / static_cast<double>(head_dim));
+    for (int32_t p = 0; p < max_seq; ++p) {
+        float* c = cos_out + static_cast<size_t>(p) * head_dim;
+        float* sn = sin_out + static_cast<size_t>(p) * head_dim;
+        for (int32_t i = 0; i < half; ++i) {
+            const double a = static_cast<double>(p) * inv[i];
+            c[i] = c[i + half] = static_cast<float>(std::cos(a));
+            sn[i] = sn[i + half] = static_cast<float>(std::sin(a));
+        }
+    }
+    return GKV_OK;
+}
+
+int gkv_qk_norm_rope(const void* q_flat, const void* k_flat, const void* v_flat, int32_t seq_len, int32_t n_q_heads,
+                     int32_t n_kv_heads, const gkv_qk_norm* qk, int32_t start_pos, void* q_out, void* k_out,
+                     void* v_out, gkv_stream_t stream) {
+    if (!q_flat || !k_flat || !v_flat || !q_out || !k_out || !v_out || seq_len < 0 || n_q_heads < 1 || n_kv_heads < 1)
+        return fail(GKV_ERR_INVALID, "gkv_qk_norm_rope: bad arguments");
+    if (!aligned16(v_flat) || !aligned16(v_out)) return fail(GKV_ERR_INVALID, "V buffers must be 16-byte aligned");
+    int st = check_qk(qk, start_pos, seq_len);
+    if (st) return st;
+    const gkv::QkNorm n{qk->q_norm_w, qk->k_norm_w, qk->cos_tab, qk->sin_tab, qk->eps};
+    cudaError_t e = gkv::launch_qk_norm_rope(
+        static_cast<const uint16_t*>(q_flat), static_cast<const uint16_t*>(k_flat), static_cast<const uint16_t*>(v_flat),
+        seq_len, n_q_heads, n_kv_heads, n, start_pos, static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_out),
+        static_cast<uint16_t*>(v_out), reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "qk norm / rope launch");
+    return GKV_OK;
+}
+
+int gkv_paged_attention_raw_qknorm(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
+                                   const void* q_flat, const void* k_flat, const void* v_flat, void* out,
+                                   int32_t n_q_heads, int32_t seq_len, float scale, int32_t causal, int32_t out_dtype,
+                                   const gkv_qk_norm* qk, gkv_stream_t stream) {
+    int st = check_pool(pool);
+    if (st) return st;
+    if (!t || seq_len < 1 || !q_flat || !k_flat || !v_flat) return fail(GKV_ERR_INVALID, "bad arguments");
+    if ((st = check_qk(qk, n_prior, seq_len))) return st;
+    const gkv::QkNorm n{qk->q_norm_w, qk->k_norm_w, qk->cos_tab, qk->sin_tab, qk->eps};
+    if (seq_len == 1)  // [1][H*128] is already [H][1][128]: QK-norm + RoPE inside the decode kernel
+        return attention_raw(pool, t, n_prior, np, q_flat, k_flat, v_flat, out, n_q_heads, 1, scale, causal,
+                             out_dtype, &n, stream);
+    // A chunk: normalise, rotate and permute into the table's buffer, then
+    // the chunked-prefill path.
+    const size_t elems_q = static_cast<size_t>(seq_len) * n_q_heads * 128;
+    const size_t elems_kv = static_cast<size_t>(seq_len) * pool->n_kv_heads * 128;
+    const size_t bytes = (elems_q + 2 * elems_kv) * sizeof(uint16_t);
+    DeviceGuard g(t->device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", t->device);
+    if (bytes > t->qk_bytes) {
+        // The previous buffer may still be read by work queued on a stream.
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "qk buffer grow");
+        cudaFree(t->qk_buf);
+        t->qk_buf = nullptr;
+        t->qk_bytes = 0;
+        if ((e = cudaMalloc(&t->qk_buf, bytes)) != cudaSuccess) return cuda_fail(e, "qk buffer grow");
+        t->qk_bytes = bytes;
+    }
+    uint16_t* qb = static_cast<uint16_t*>(t->qk_buf);
+    uint16_t* kb = qb + elems_q;
+    uint16_t* vb = kb + elems_kv;
+    if ((st = gkv_qk_norm_rope(q_flat, k_flat, v_flat, seq_len, n_q_heads, pool->n_kv_heads, qk, n_prior, qb, kb, vb,
+                               stream)))
+        return st;
+    return attention_raw(pool, t, n_prior, np, qb, kb, vb, out, n_q_heads, seq_len, scale, causal, out_dtype, nullptr,
+                         stream);
 }
 
 }  // extern "C"
@@ -771,6 +880,30 @@ int gkv_paged_attention(gkv_manager* m, int32_t layer_id, const void* Q, const v
     gkv_new_pages np = pending(*L);
     st = gkv_paged_attention_raw(&pool, L->table, L->num_cached, &np, Q, K, V, out, n_q_heads, seq_len, scale,
                                  causal, out_dtype, stream);
+    if (st) {
+        ungrow(*L, first);
+        return st;
+    }
+    L->on_device = static_cast<int32_t>(L->k_ids.size());
+    L->num_cached += seq_len;
+    return GKV_OK;
+}
+
+int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_flat, const void* k_flat,
+                               const void* v_flat, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
+                               int32_t causal, int32_t out_dtype, const gkv_qk_norm* qk, gkv_stream_t stream) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    if (L->head_dim != 128 || L->dtype != GKV_BF16)
+        return fail(GKV_ERR_UNSUPPORTED, "QK-norm + RoPE is built for head_dim 128, bf16");
+    if (seq_len < 1) return fail(GKV_ERR_INVALID, "seq_len %d", seq_len);
+    int32_t first = 0, n = 0;
+    if ((st = grow(*L, seq_len, &first, &n))) return st;
+    gkv_pool_desc pool = pool_of(*L);
+    gkv_new_pages np = pending(*L);
+    st = gkv_paged_attention_raw_qknorm(&pool, L->table, L->num_cached, &np, q_flat, k_flat, v_flat, out, n_q_heads,
+                                        seq_len, scale, causal, out_dtype, qk, stream);
     if (st) {
         ungrow(*L, first);
         return st;

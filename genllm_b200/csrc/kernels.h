@@ -37,6 +37,15 @@ struct PoolView {
 };
 
 
+// QK-norm + RoPE parameters (qk_rope.cuh): device pointers and eps.
+struct QkNorm {
+    const float* q_w;  // [128] fp32 RMSNorm weights of Q heads
+    const float* k_w;  // [128] of K heads
+    const float* cos;  // [max_seq][128] fp32 RoPE table (both halves equal)
+    const float* sin;
+    float eps;
+};
+
 struct DecodeLaunch {
     const uint16_t* q;      // [Hq][128]
     const uint16_t* k_new;  // [Hkv][128] token appended by this step (or null)
@@ -49,6 +58,7 @@ struct DecodeLaunch {
     int32_t n_pages;        // logical pages covering `total`
     float scale;
     int32_t n_splits;       // 0 = choose
+    const QkNorm* qk;       // non-null: q / k_new are pre-norm; QK-norm + RoPE fused (position n_prior)
 };
 
 // Head all-gather fused into the split combine (multi-GPU KV-head sharding):
@@ -94,6 +104,12 @@ struct PrefillLaunch {
     float scale;
     int32_t causal;
 };
+
+// Per-head QK-norm + RoPE of Q and K and the head-major permute of Q, K and
+// V, in one launch (qk_rope.cu): [S][H*128] in, [H][S][128] out.
+cudaError_t launch_qk_norm_rope(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t seq_len,
+                                int32_t n_q_heads, int32_t n_kv_heads, const QkNorm& n, int32_t start_pos,
+                                uint16_t* q_out, uint16_t* k_out, uint16_t* v_out, cudaStream_t stream);
 
 // Record the message gkv_last_error() returns on this host thread.
 void set_last_error(const char* msg);

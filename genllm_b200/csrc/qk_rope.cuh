@@ -1,0 +1,60 @@
+// qk_rope.cuh — per-head RMSNorm (Qwen3's QK-norm) and RoPE of one 128-dim
+// row by one warp, bit-exact with the reference CPU ops:
+//   src/backend/cpu/normalization.cpp:39-95  rms_norm (AVX2): four 8-lane
+//     fma accumulators over 32-element steps, merged (a0+a1)+(a2+a3), the
+//     two 128-bit halves added, two horizontal adds; rms = 1/sqrt(sum/n+eps);
+//     (x * rms) * w stored by truncation to bf16;
+//   src/backend/cpu/rope.cpp:73-110  ApplyRopeImpl<CPU>: half-split
+//     rotation with cos/sin of position pos; as the reference is built
+//     (-O3 -mfma, GCC's default contraction for C++) each rotation is one
+//     fused multiply-add whose addend is the other product rounded; bf16 RNE
+//     store.
+// Lane l holds the row's elements l, l+32, l+64, l+96 (index `it`): that is
+// the AVX2 accumulator layout (lane = 8 k + j for accumulator k, lane j) and
+// puts each RoPE pair (i, i+64) in one lane.
+#pragma once
+#include <stdint.h>
+
+#include "device.cuh"
+#include "kernels.h"
+
+namespace gkv {
+
+// x: this lane's 4 elements (floats of bf16 inputs); w: the weights; cs/sn:
+// the position's cos/sin rows. out: bf16 bits of the same 4 elements.
+__device__ __forceinline__ void norm_rope_row(const float (&x)[4], int lane, const float* w, const float* cs,
+                                              const float* sn, float eps, uint16_t (&out)[4]) {
+    // Sum of squares in the AVX2 order.
+    float acc = 0.f;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) acc = __fmaf_rn(x[it], x[it], acc);
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xFFFFFFFFu, acc, 8));  // lanes 0-7: a0+a1, 16-23: a2+a3
+    const float a0 = __fadd_rn(t, __shfl_down_sync(0xFFFFFFFFu, t, 16));    // lanes 0-7
+    const float s4 = __fadd_rn(a0, __shfl_down_sync(0xFFFFFFFFu, a0, 4));   // lanes 0-3
+    const float u = __fadd_rn(s4, __shfl_down_sync(0xFFFFFFFFu, s4, 1));    // lanes 0, 2
+    const float tot = __fadd_rn(u, __shfl_down_sync(0xFFFFFFFFu, u, 2));    // lane 0
+    const float sum = __shfl_sync(0xFFFFFFFFu, tot, 0);
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), eps)));
+    float y[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const float v = __fmul_rn(__fmul_rn(x[it], rms), w[lane + 32 * it]);
+        y[it] = __uint_as_float(__float_as_uint(v) & 0xFFFF0000u);  // truncation to bf16
+    }
+    // RoPE: pairs (it, it + 2) = elements (i, i + 64), i = lane + 32 it.
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int i = lane + 32 * it;
+        const float c = cs[i], s = sn[i];
+        out[it] = bf16_bits_ref(__fmaf_rn(y[it], c, -__fmul_rn(y[it + 2], s)));
+        out[it + 2] = bf16_bits_ref(__fmaf_rn(y[it], s, __fmul_rn(y[it + 2], c)));
+    }
+}
+
+// Load a bf16 row's 4 elements of this lane.
+__device__ __forceinline__ void load_row4(const uint16_t* row, int lane, float (&x)[4]) {
+#pragma unroll
+    for (int it = 0; it < 4; ++it) x[it] = __uint_as_float((uint32_t)row[lane + 32 * it] << 16);
+}
+
+}  // namespace gkv

@@ -257,3 +257,76 @@ def paged_attention(manager: PagedAttentionManager, layer_id: int, Q: torch.Tens
                                     1 if causal else 0, groups, _TORCH_TO_GKV[Q.dtype], _TORCH_TO_GKV[out.dtype],
                                     _stream_handle(manager.device, stream)))
     return out
+
+
+def rope_cache(theta: float, head_dim: int, max_seq: int):
+    """``RopeCacheImpl<CPU>`` tables [max_seq, head_dim] fp32 (host numpy),
+    computed by the library (gkv_rope_cache)."""
+    import numpy as np
+    cos = np.empty((max_seq, head_dim), dtype=np.float32)
+    sin = np.empty((max_seq, head_dim), dtype=np.float32)
+    check(lib().gkv_rope_cache(float(theta), head_dim, max_seq, C.c_void_p(cos.ctypes.data),
+                               C.c_void_p(sin.ctypes.data)))
+    return cos, sin
+
+
+class QkNorm:
+    """Qwen3's per-head QK-norm + RoPE parameters on a device: the two
+    RMSNorm weights [128] fp32, eps and the RoPE tables for max_seq positions.
+    """
+
+    def __init__(self, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, eps: float, theta: float, max_seq: int,
+                 device: int | torch.device = 0):
+        dev = torch.device("cuda", device) if isinstance(device, int) else device
+        cos, sin = rope_cache(theta, 128, max_seq)
+        self.q_w = q_norm_w.to(device=dev, dtype=torch.float32).contiguous()
+        self.k_w = k_norm_w.to(device=dev, dtype=torch.float32).contiguous()
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        self.eps = float(eps)
+        self.max_seq = max_seq
+        self.desc = _lib.QkNormDesc(self.q_w.data_ptr(), self.k_w.data_ptr(), self.cos.data_ptr(),
+                                    self.sin.data_ptr(), max_seq, self.eps)
+
+
+def qk_norm_rope(q_flat: torch.Tensor, k_flat: torch.Tensor, v_flat: torch.Tensor, n_q_heads: int,
+                 n_kv_heads: int, qk: QkNorm, start_pos: int, stream=None):
+    """[S, H*128] projections -> ([Hq, S, 128], [Hkv, S, 128], [Hkv, S, 128])
+    bf16: QK-norm + RoPE of Q and K, head-major permute of all three, in one
+    launch (gkv_qk_norm_rope)."""
+    S = q_flat.shape[0]
+    dev = q_flat.device
+    q = torch.empty((n_q_heads, S, 128), dtype=torch.bfloat16, device=dev)
+    k = torch.empty((n_kv_heads, S, 128), dtype=torch.bfloat16, device=dev)
+    v = torch.empty((n_kv_heads, S, 128), dtype=torch.bfloat16, device=dev)
+    for t in (q_flat, k_flat, v_flat):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise GkvError(_lib.GKV_ERR_INVALID, "projections must be contiguous bf16")
+    check(lib().gkv_qk_norm_rope(C.c_void_p(q_flat.data_ptr()), C.c_void_p(k_flat.data_ptr()),
+                                 C.c_void_p(v_flat.data_ptr()), S, n_q_heads, n_kv_heads, C.byref(qk.desc),
+                                 start_pos, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                                 C.c_void_p(v.data_ptr()), _stream_handle(dev, stream)))
+    return q, k, v
+
+
+def paged_attention_qknorm(manager: PagedAttentionManager, layer_id: int, q_flat: torch.Tensor,
+                           k_flat: torch.Tensor, v_flat: torch.Tensor, n_q_heads: int, qk: QkNorm,
+                           out: Optional[torch.Tensor] = None, scale: Optional[float] = None, causal: bool = True,
+                           stream=None) -> torch.Tensor:
+    """The attention op on the Q/K/V projections ([S, H*128] bf16): QK-norm +
+    RoPE at the layer's next positions, append, attend — one launch for a
+    decode step (gkv_paged_attention_qknorm). out: [Hq, S, 128]."""
+    S = q_flat.shape[0]
+    if out is None:
+        out = torch.empty((n_q_heads, S, 128), dtype=torch.bfloat16, device=q_flat.device)
+    sc = float(scale) if scale is not None else 1.0 / 128.0 ** 0.5
+    for t in (q_flat, k_flat, v_flat, out):
+        if not t.is_contiguous() or t.device != manager.device:
+            raise GkvError(_lib.GKV_ERR_INVALID, "tensors must be contiguous and on the manager's device")
+    check(lib().gkv_paged_attention_qknorm(manager.handle, layer_id, C.c_void_p(q_flat.data_ptr()),
+                                           C.c_void_p(k_flat.data_ptr()), C.c_void_p(v_flat.data_ptr()),
+                                           C.c_void_p(out.data_ptr()), n_q_heads, S, sc, 1 if causal else 0,
+                                           _TORCH_TO_GKV[out.dtype], C.byref(qk.desc),
+                                           _stream_handle(manager.device, stream)))
+    return out
+

@@ -293,6 +293,56 @@ int gkv_paged_decode_static_scratch(const gkv_pool_desc* pool, const int32_t* de
                                     void* out, int32_t n_q_heads, float scale, int32_t out_dtype,
                                     gkv_stream_t stream);
 
+/* ---------------- QK-norm + RoPE (the step feeding the append) -------------
+ * Qwen3's attention block turns the Q/K/V projections [S][H*128] into the
+ * post-QK-norm, post-RoPE Q and K the paged-attention op appends and attends
+ * (src/model/Qwen3.cpp:136-154: reshape_permute x3, rms_norm x2 with the
+ * per-head weights attn_q_norm / attn_k_norm, apply_rope x2). These entry
+ * points fuse that step: standalone (one launch instead of seven), or inside
+ * the attention call itself (decode: no launch of its own). Results are
+ * bit-exact with the reference CPU ops (RmsNormImpl / ApplyRopeImpl<CPU>,
+ * src/backend/cpu/normalization.cpp, src/backend/cpu/rope.cpp). head_dim 128. */
+typedef struct gkv_qk_norm {
+    const float* q_norm_w; /* device, [128] fp32 (blk.N.attn_q_norm.weight) */
+    const float* k_norm_w; /* device, [128] fp32 (blk.N.attn_k_norm.weight) */
+    const float* cos_tab;  /* device, [max_seq][128] fp32, from gkv_rope_cache */
+    const float* sin_tab;
+    int32_t max_seq;       /* rows of the tables; positions must stay below */
+    float eps;             /* rms_norm_eps */
+} gkv_qk_norm;
+
+/* Host: the RoPE cos/sin tables [max_seq][head_dim] fp32 into host arrays, as
+ * RopeCacheImpl<CPU>::execute (src/backend/cpu/rope.cpp:112-140) fills them
+ * (double-precision angles; both halves of a row equal). */
+int gkv_rope_cache(float theta, int32_t head_dim, int32_t max_seq, float* cos_out, float* sin_out);
+
+/* Device: q_flat [S][Hq*128], k_flat / v_flat [S][Hkv*128] bf16 ->
+ * q_out [Hq][S][128] (norm + RoPE), k_out [Hkv][S][128] (norm + RoPE),
+ * v_out [Hkv][S][128] (permute only); token s sits at position start_pos + s.
+ * Replaces ApplyRopeImpl<CUDA>::execute (src/backend/cuda/rope.cu:52-111),
+ * RmsNormImpl<CUDA>::execute (src/backend/cuda/normalization.cu:49-90) on
+ * the heads and PermuteImpl<CUDA>::execute (src/backend/cuda/shape.cu:45) x3.
+ * Allocates nothing. */
+int gkv_qk_norm_rope(const void* q_flat, const void* k_flat, const void* v_flat, int32_t seq_len,
+                     int32_t n_q_heads, int32_t n_kv_heads, const gkv_qk_norm* qk, int32_t start_pos,
+                     void* q_out, void* k_out, void* v_out, gkv_stream_t stream);
+
+/* gkv_paged_attention_raw on the projections: Q, K, V as q_flat / k_flat /
+ * v_flat above, QK-norm + RoPE applied at positions n_prior + s. seq_len 1
+ * fuses it into the decode kernel; longer chunks run gkv_qk_norm_rope into a
+ * buffer the table owns (grown on demand), then the chunked-prefill path. */
+int gkv_paged_attention_raw_qknorm(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior,
+                                   const gkv_new_pages* np, const void* q_flat, const void* k_flat,
+                                   const void* v_flat, void* out, int32_t n_q_heads, int32_t seq_len,
+                                   float scale, int32_t causal, int32_t out_dtype, const gkv_qk_norm* qk,
+                                   gkv_stream_t stream);
+
+/* The managed tier's gkv_paged_attention on the projections (positions =
+ * the layer's cached token count), batch 1, head_dim 128. */
+int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_flat, const void* k_flat,
+                               const void* v_flat, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
+                               int32_t causal, int32_t out_dtype, const gkv_qk_norm* qk, gkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,3 +70,15 @@ def test_apply_rope_live(seed, start):
     if start + 33 > 40960:
         start = 40960 - 33
     assert np.array_equal(ORC.apply_rope_bf16(x, cos, sin, start), R.apply_rope_bf16(x, cos, sin, start))
+
+
+@pytest.mark.parametrize("name,kw,max_seq", QK_ROPE)
+def test_library_rope_cache_matches_reference(name, kw, max_seq):
+    """gkv_rope_cache (the product's host-side table builder) against the
+    reference's table checksums in the fixtures."""
+    from genllm_b200.paged_attention import rope_cache
+    z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    c = qk_rope_case(**kw)
+    cos, sin = rope_cache(c.theta, c.head_dim, max_seq)
+    assert [sha(cos), sha(sin)] == [str(s) for s in z["cache_sha"]]
+
