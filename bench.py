@@ -49,8 +49,9 @@ def parse():
     ap.add_argument("--pool", type=int, default=0, help="pages per pool (0: max(4096, ctx/16 + 64))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor cores")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qknorm"],
+                    help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor "
+                         "cores; qknorm: config 3 fed the Q/K/V projections, QK-norm + RoPE fused into the step")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: head all-gather fused into the decode (NVLink peer stores) or NCCL all_gather")
     ap.add_argument("--no-kernel-events", action="store_true",
@@ -305,6 +306,127 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+def run_qknorm(args):
+    """Config 3 on the projections: each layer-token's Q/K/V arrive as the
+    Q/K/V projections ([1, H*128] bf16) and go through QK-norm + RoPE before
+    the append and the attention (src/model/Qwen3.cpp:136-158). Fused: one
+    gkv_paged_attention_qknorm per layer (the norm and rotation run inside
+    the decode kernel). Unfused: gkv_qk_norm_rope (one launch for the
+    permutes, norms and rotations the reference runs as seven ops) then
+    gkv_paged_attention. Both are timed; `value` is the fused one."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from genllm_b200 import _lib
+    from genllm_b200.paged_attention import QkNorm
+    from genllm_b200.workload import DecodeWorkload
+
+    torch.cuda.set_device(0)
+    wl = DecodeWorkload(0, n_layers=args.layers, ctx=args.ctx, pool_pages=pool_pages(args), n_q_heads=HQ,
+                        n_kv_heads=HKV, head_dim=D, seed=0)
+    g = torch.Generator().manual_seed(5)
+    max_seq = args.ctx + 2 * (args.steps + args.warmup) + 64
+    qk = QkNorm(1 + 0.25 * torch.randn(D, generator=g), 1 + 0.25 * torch.randn(D, generator=g), 1e-6, 1e6,
+                max_seq, 0)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+    tq = torch.empty((HQ, 1, D), dtype=torch.bfloat16, device="cuda")
+    tk = torch.empty((HKV, 1, D), dtype=torch.bfloat16, device="cuda")
+    tv = torch.empty((HKV, 1, D), dtype=torch.bfloat16, device="cuda")
+    sc = C.c_float(1.0 / D ** 0.5)
+
+    def fused_step():
+        for l, b in enumerate(wl.layers):
+            _lib.check(L.gkv_paged_attention_qknorm(wl.mgr.handle, l, C.c_void_p(b.q.data_ptr()),
+                                                    C.c_void_p(b.k.data_ptr()), C.c_void_p(b.v.data_ptr()),
+                                                    C.c_void_p(b.out.data_ptr()), HQ, 1, sc, 1, _lib.GKV_BF16,
+                                                    C.byref(qk.desc), sh))
+
+    pos = [args.ctx]  # every layer holds the same number of tokens
+
+    def unfused_step():
+        for l, b in enumerate(wl.layers):
+            _lib.check(L.gkv_qk_norm_rope(C.c_void_p(b.q.data_ptr()), C.c_void_p(b.k.data_ptr()),
+                                          C.c_void_p(b.v.data_ptr()), 1, HQ, HKV, C.byref(qk.desc), pos[0],
+                                          C.c_void_p(tq.data_ptr()), C.c_void_p(tk.data_ptr()),
+                                          C.c_void_p(tv.data_ptr()), sh))
+            _lib.check(L.gkv_paged_attention(wl.mgr.handle, l, C.c_void_p(tq.data_ptr()), C.c_void_p(tk.data_ptr()),
+                                             C.c_void_p(tv.data_ptr()), C.c_void_p(b.out.data_ptr()), 1, HQ, 1, D,
+                                             HKV, sc, 1, HQ // HKV, _lib.GKV_BF16, _lib.GKV_BF16, sh))
+        pos[0] += 1
+
+    def counted_fused():
+        fused_step()
+        pos[0] += 1
+
+    def plain_step():
+        for l in range(args.layers):
+            wl.layer_step(l, sh)
+        pos[0] += 1
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms_fused = timed(counted_fused)
+    clk = clocks.stop()
+    ms_unfused = timed(unfused_step)
+    ms_plain = timed(plain_step)
+    per_layer = ms_fused * 1e3 / args.layers
+    ctx_now = wl.mgr.get_layer(0).num_cached
+    bytes_lt = 2 * ctx_now * HKV * D * 2 + HQ * D * 2 * 2 + 2 * HKV * D * 2
+    gbs = bytes_lt / (per_layer * 1e-6) / 1e9
+    peak, src = measured_peak()
+    cpu = None
+    try:
+        from oracle.oracle import RefOps
+        from genllm_b200.synth import randn_bf16
+        R = RefOps()
+        rng = np.random.default_rng(0)
+        cos, sin = R.rope_cache(1e6, D, 64)
+        xq = randn_bf16(rng, (HQ, 1, D))
+        xk = randn_bf16(rng, (HKV, 1, D))
+        wq = np.ones(D, np.float32)
+        n = 2000
+        t0 = time.perf_counter()
+        for _ in range(n):
+            R.apply_rope_bf16(R.rms_norm_bf16(xq, wq, 1e-6), cos, sin, 5)
+            R.apply_rope_bf16(R.rms_norm_bf16(xk, wq, 1e-6), cos, sin, 5)
+        us = (time.perf_counter() - t0) / n * 1e6
+        cpu = {"value": round(us, 2), "unit": "us per layer-token (QK-norm + RoPE only)", "cores": 1,
+               "kind": "reference", "sample": f"{n} layer-tokens of the reference CPU rms_norm + apply_rope ops "
+                                               "(Hq 32, Hkv 8), ctypes call overhead included"}
+    except Exception as exc:  # noqa: BLE001
+        cpu = {"unavailable": str(exc)[:200]}
+    line = {"metric": "paged-attn decode on the Q/K/V projections (QK-norm + RoPE + append + attention), "
+                      "us per layer-token @32k; Qwen3-4B shape",
+            "value": round(per_layer, 3), "unit": "us/layer-token", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_fused, 4), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 3 fed the projections: 36 layers at 32k, per layer-token QK-norm "
+                                   "(RMSNorm eps 1e-6) + RoPE (theta 1e6) + append + decode",
+                       "n_q_heads": HQ, "n_kv_heads": HKV, "head_dim": D, "l2": "KV of a step (4.8 GB) >> L2"},
+            "unfused_us_per_layer_token": round(ms_unfused * 1e3 / args.layers, 3),
+            "plain_decode_us_per_layer_token": round(ms_plain * 1e3 / args.layers, 3),
+            "gpu_launches": 2 * args.layers * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "peak_source": src,
+                         "kernel": "paged_decode_kernel (QK-norm + RoPE fused) + combine, whole layer-token"},
+            "cpu_baseline": cpu, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -316,6 +438,9 @@ def main():
         return
     if args.workload == "prefill":
         run_prefill(args)
+        return
+    if args.workload == "qknorm":
+        run_qknorm(args)
         return
 
     import torch

@@ -141,6 +141,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     PROBE_T(0);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    if (a.qk_on && threadIdx.x < 16) {
+        // The QK-norm weights and this position's RoPE rows are not the
+        // previous kernel's outputs: pull them toward L2 before this CTA's
+        // page stream starts, so that the loads after griddepcontrol.wait do
+        // not queue behind it.
+        const size_t pos = (size_t)a.n_prior * kHeadDim;
+        const float* src = lane < 4 ? a.qk.cos + pos : lane < 8 ? a.qk.sin + pos : lane < 12 ? a.qk.q_w : a.qk.k_w;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + (lane & 3) * 32));
+    }
     const int split = blockIdx.x;
     const int Hkv = a.n_kv_heads;
     const int G = a.group;
@@ -229,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // (programmatic dependent launch): the page stream above reads only
         // cached pages, but Q and the new K/V row are that kernel's outputs.
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        PROBE_T(5);
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
         uint32_t qb[8][2];
         if (a.qk_on) {
@@ -238,28 +248,47 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) qb[kk][0] = qb[kk][1] = 0u;
             if (active) {
-                float xq[8][4];
-#pragma unroll
-                for (int n = 0; n < 8; ++n)
-                    if (n < G) load_row4(a.q + (size_t)(head * G + n) * kHeadDim, lane, xq[n]);
+                // One query row per 8-lane group, four rows at once
+                // (norm_rope_row_g8), then each row through a staging row of
+                // the warp's 512-byte P buffer (idle until the first page),
+                // two at a time, from which each lane takes its fragment.
+                const int grp = lane >> 3, j = lane & 7;
                 const size_t pos = (size_t)a.n_prior * kHeadDim;
                 uint16_t* stage = reinterpret_cast<uint16_t*>(pbuf);
 #pragma unroll
-                for (int n = 0; n < 8; ++n) {
-                    if (n >= G) break;
-                    uint16_t o[4];
-                    norm_rope_row(xq[n], lane, a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, a.qk.eps, o);
+                for (int b0 = 0; b0 < 8; b0 += 4) {
+                    if (b0 >= G) break;
+                    const int n = b0 + grp;
+                    const bool row_ok = n < G;
+                    const uint16_t* qr = a.q + (size_t)(head * G + (row_ok ? n : 0)) * kHeadDim;
+                    float x[4][4];
 #pragma unroll
-                    for (int it = 0; it < 4; ++it) stage[lane + 32 * it] = o[it];
-                    __syncwarp();
-                    if (g == n) {
+                    for (int it = 0; it < 4; ++it)
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            qb[kk][0] = *reinterpret_cast<const uint32_t*>(stage + kk * 16 + 2 * t);
-                            qb[kk][1] = *reinterpret_cast<const uint32_t*>(stage + kk * 16 + 2 * t + 8);
+                        for (int k = 0; k < 4; ++k)
+                            x[it][k] = __uint_as_float((uint32_t)qr[32 * it + 8 * k + j] << 16);
+                    uint16_t o[4][4];
+                    norm_rope_row_g8(x, j, a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, a.qk.eps, o);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {  // groups 2 half, 2 half + 1 -> staging rows 0, 1
+                        if ((grp >> 1) == half && row_ok) {
+#pragma unroll
+                            for (int it = 0; it < 4; ++it)
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) stage[(grp & 1) * kHeadDim + 32 * it + 8 * k + j] = o[it][k];
                         }
+                        __syncwarp();
+                        const int r0 = b0 + 2 * half;
+                        if ((g == r0 || g == r0 + 1) && g < G) {
+                            const uint16_t* row = stage + (g - r0) * kHeadDim;
+#pragma unroll
+                            for (int kk = 0; kk < 8; ++kk) {
+                                qb[kk][0] = *reinterpret_cast<const uint32_t*>(row + kk * 16 + 2 * t);
+                                qb[kk][1] = *reinterpret_cast<const uint32_t*>(row + kk * 16 + 2 * t + 8);
+                            }
+                        }
+                        __syncwarp();
                     }
-                    __syncwarp();
                 }
             }
         } else {
@@ -272,6 +301,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                 qb[kk][1] = valid ? *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 2 * t + 8) : 0u;
             }
         }
+#ifdef GKV_PROBE_TIMELINE
+        asm volatile("" ::"r"(qb[0][0]), "r"(qb[7][1]));
+        PROBE_T(6);
+#endif
         float acc[8][4];
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
@@ -308,8 +341,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                         float xk[4];
                         load_row4(a.k_new + (size_t)head * kHeadDim, lane, xk);
                         const size_t pos = (size_t)a.n_prior * kHeadDim;
+                        const RowParams rp = load_row_params(a.qk.k_w, a.qk.cos + pos, a.qk.sin + pos, lane);
                         uint16_t o[4];
-                        norm_rope_row(xk, lane, a.qk.k_w, a.qk.cos + pos, a.qk.sin + pos, a.qk.eps, o);
+                        norm_rope_row(xk, rp, a.qk.eps, o);
                         uint16_t* stage = reinterpret_cast<uint16_t*>(pbuf);
 #pragma unroll
                         for (int it = 0; it < 4; ++it) stage[lane + 32 * it] = o[it];

@@ -59,8 +59,9 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_kernel(const QkRopeP
     float x[4];
     load_row4(src, lane, x);
     const size_t pos = (size_t)(a.start_pos + s) * kHeadDim;
+    const RowParams rp = load_row_params(kind == 0 ? a.n.q_w : a.n.k_w, a.n.cos + pos, a.n.sin + pos, lane);
     uint16_t o[4];
-    norm_rope_row(x, lane, kind == 0 ? a.n.q_w : a.n.k_w, a.n.cos + pos, a.n.sin + pos, a.n.eps, o);
+    norm_rope_row(x, rp, a.n.eps, o);
 #pragma unroll
     for (int it = 0; it < 4; ++it) dst[lane + 32 * it] = o[it];
 }
