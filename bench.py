@@ -552,8 +552,20 @@ def main():
     h_in.copy_(wl.inbuf)
     h_out = torch.empty((args.layers, (HQ if world > 1 else hq_l) * D), dtype=torch.bfloat16).pin_memory()
 
+    from genllm_b200.paged_attention import DecodeStep
+    one_call = None
+    if hg is None and world == 1:
+        # The whole step's 36 layers through one library call.
+        one_call = DecodeStep(wl.mgr, list(range(args.layers)), [b.q for b in wl.layers], [b.k for b in wl.layers],
+                              [b.v for b in wl.layers], [b.out for b in wl.layers], hq_l, wl.scale)
+
     def e2e_step():
         wl.inbuf.copy_(h_in, non_blocking=True)
+        if one_call is not None:
+            one_call.run()
+            h_out.copy_(wl.outbuf, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return float(h_out[-1, 0])
         for l in range(args.layers):
             L = wl.layers[l]
             if hg is not None:
@@ -592,7 +604,13 @@ def main():
     d2h = h_out.numel() * 2
 
     peak, peak_src = measured_peak()
-    achieved = (kern_bytes or per_launch_bytes) / (kern_max / 1e3) / 1e9
+    # Per launch pair (decode + combine of one layer), averaged over the
+    # timed region (CUDA events around the K timed steps, launches
+    # overlapping as they do in use); the instrumented per-launch pass (events
+    # between launches serialise them) is reported beside it.
+    pair_ms = ms_max / (args.steps * args.layers)
+    achieved = per_launch_bytes / (pair_ms / 1e3) / 1e9
+    serialized = (kern_bytes or per_launch_bytes) / (kern_max / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -603,7 +621,10 @@ def main():
         "tok_per_s_qwen3_4b_attention": round(args.steps / (ms_max / 1e3), 2),
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps, "ms_per_step": round(te.item() / e2e_steps, 4),
-                "path": "one pinned H2D copy of all layers Q/K/V, 36 genllm_b200.paged_attention calls (C ABI), one D2H copy of the outputs, host reads the result"},
+                "path": ("one pinned H2D copy of all layers Q/K/V, one gkv_decode_layers call (C ABI) for the 36 "
+                         "layers, one D2H copy of the outputs, host reads the result" if one_call is not None else
+                         "one pinned H2D copy of all layers Q/K/V, per-layer C ABI calls, one D2H copy of the "
+                         "outputs, host reads the result")},
         "gpu_launches": 2 * args.steps * args.layers,
         "gather": (args.gather if world > 1 else None),
         "host_enqueue_ms_per_step": round(1e3 * host_enqueue_s / args.steps, 4),
@@ -613,8 +634,11 @@ def main():
                                        "(profiles/paged_decode_kernel_qwen3_4b_32k.md)",
                      "peak_source": peak_src,
                      "kernel": "paged_decode_kernel + paged_decode_combine_kernel (one decode step of one layer)",
-                     "kernel_avg_us": round(1e3 * kern_max, 3),
-                     "bytes_per_launch": round(per_launch_bytes)},
+                     "kernel_avg_us": round(1e3 * pair_ms, 3),
+                     "bytes_per_launch": round(per_launch_bytes),
+                     "serialized_launch": {"avg_us": round(1e3 * kern_max, 3), "achieved": round(serialized, 1),
+                                           "how": "separate pass, CUDA events recorded between launches (no "
+                                                  "overlap of consecutive launches)"}},
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

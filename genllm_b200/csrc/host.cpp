@@ -913,6 +913,23 @@ int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_f
     return GKV_OK;
 }
 
+int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids, const void* const* Q,
+                      const void* const* K, const void* const* V, void* const* out, int32_t n_q_heads, float scale,
+                      int32_t out_dtype, gkv_stream_t stream) {
+    if (!m || n_layers < 0 || (n_layers && (!layer_ids || !Q || !K || !V || !out)))
+        return fail(GKV_ERR_INVALID, "gkv_decode_layers: bad arguments");
+    for (int32_t i = 0; i < n_layers; ++i) {
+        Layer* L = nullptr;
+        int st = ready_layer(m, layer_ids[i], &L);
+        if (st) return st;
+        if (n_q_heads % L->n_kv_heads) return fail(GKV_ERR_INVALID, "n_q_heads %d, n_kv_heads %d", n_q_heads, L->n_kv_heads);
+        st = gkv_paged_attention(m, layer_ids[i], Q[i], K[i], V[i], out[i], 1, n_q_heads, 1, L->head_dim,
+                                 L->n_kv_heads, scale, 1, n_q_heads / L->n_kv_heads, L->dtype, out_dtype, stream);
+        if (st) return st;
+    }
+    return GKV_OK;
+}
+
 int gkv_reset_layer(gkv_manager* m, int32_t layer_id) {
     Layer* L = find_layer(m, layer_id);
     if (!L) return fail(GKV_ERR_STATE, "layer %d unknown", layer_id);

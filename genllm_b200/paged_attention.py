@@ -330,3 +330,30 @@ def paged_attention_qknorm(manager: PagedAttentionManager, layer_id: int, q_flat
                                            _stream_handle(manager.device, stream)))
     return out
 
+
+class DecodeStep:
+    """One decode token through a fixed list of layers with one library call
+    (gkv_decode_layers). The tensors are bound once: Q [Hq, 128] and K, V
+    [Hkv, 128] per layer (any views of device memory), out [Hq, 128]; each
+    ``run()`` appends one token to every layer and attends."""
+
+    def __init__(self, manager: PagedAttentionManager, layer_ids, Qs, Ks, Vs, outs, n_q_heads: int,
+                 scale: Optional[float] = None):
+        n = len(layer_ids)
+        self.manager = manager
+        self._keep = (list(Qs), list(Ks), list(Vs), list(outs))
+        for group in self._keep:
+            if len(group) != n or any((not t.is_contiguous()) or t.device != manager.device for t in group):
+                raise GkvError(_lib.GKV_ERR_INVALID, "one contiguous tensor per layer, on the manager's device")
+        self._ids = (C.c_int32 * n)(*layer_ids)
+        arr = lambda ts: (C.c_void_p * n)(*[t.data_ptr() for t in ts])  # noqa: E731
+        self._q, self._k, self._v, self._o = (arr(t) for t in self._keep)
+        self._n = n
+        self._hq = n_q_heads
+        self._scale = float(scale) if scale is not None else 1.0 / 128.0 ** 0.5
+        self._odt = _TORCH_TO_GKV[self._keep[3][0].dtype] if n else GKV_BF16
+
+    def run(self, stream=None) -> None:
+        check(lib().gkv_decode_layers(self.manager.handle, self._n, self._ids, self._q, self._k, self._v, self._o,
+                                      self._hq, self._scale, self._odt, _stream_handle(self.manager.device, stream)))
+

@@ -123,6 +123,18 @@ int gkv_paged_attention(gkv_manager* m, int32_t layer_id, const void* Q, const v
                         int32_t causal, int32_t n_kv_groups, int32_t dtype, int32_t out_dtype,
                         gkv_stream_t stream);
 
+/* One decode token through n_layers layers in one call: gkv_paged_attention
+ * (seq_len 1, causal, batch 1) on layer_ids[i] with Q[i], K[i], V[i], out[i]
+ * (device pointers, arrays of n_layers), in order on one stream. The layers
+ * are independent here (the host drives the layer-to-layer data flow), so
+ * this is a launch loop in the library: one host call per step instead of one
+ * per layer, the executor's per-op host cost gone (the reference executor
+ * synchronises the device after every op, src/core/executor.cpp:169-172).
+ * Stops at the first failing layer (layers before it have advanced). */
+int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids, const void* const* Q,
+                      const void* const* K, const void* const* V, void* const* out, int32_t n_q_heads,
+                      float scale, int32_t out_dtype, gkv_stream_t stream);
+
 /* reset (page_attention.cpp:209-216) for every layer, or one layer. Host
  * bookkeeping only: num_cached = 0, empty table, every page handed out so far
  * back on the free list in ascending order. */

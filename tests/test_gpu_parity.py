@@ -340,3 +340,35 @@ def test_prefill_page_runs(order, n_prior, n_new, causal):
                            poison_unused=True, page_order=order)
     check_case(case, causal)
 
+
+
+def test_decode_layers_one_call_matches_per_layer_calls():
+    """gkv_decode_layers (one host call for a token through several layers)
+    launches exactly what per-layer gkv_paged_attention calls launch."""
+    from genllm_b200.paged_attention import DecodeStep
+    cases = [fragmented_case(900 + l, 16, 8, 128, 300 + 37 * l, 40) for l in range(3)]
+    ma = PagedAttentionManager(0)
+    mb = PagedAttentionManager(0)
+    outs_a, outs_b, ins = [], [], []
+    for l, c in enumerate(cases):
+        build_state(c, mgr=ma, layer=l)
+        build_state(c, mgr=mb, layer=l)
+        q = to_dev_bf16(c.q, ma.device).view(16, 128)
+        k = to_dev_bf16(c.k_new, ma.device).view(8, 128)
+        v = to_dev_bf16(c.v_new, ma.device).view(8, 128)
+        ins.append((q, k, v))
+        outs_a.append(torch.empty((16, 128), dtype=torch.bfloat16, device=ma.device))
+        outs_b.append(torch.empty((1, 16, 1, 128), dtype=torch.bfloat16, device=mb.device))
+    step = DecodeStep(ma, [0, 1, 2], [i[0] for i in ins], [i[1] for i in ins], [i[2] for i in ins], outs_a, 16,
+                      cases[0].scale)
+    step.run()
+    for l, (q, k, v) in enumerate(ins):
+        paged_attention(mb, l, q.view(1, 16, 1, 128), k.view(1, 8, 1, 128), v.view(1, 8, 1, 128), out=outs_b[l],
+                        scale=cases[0].scale)
+    torch.cuda.synchronize()
+    for l in range(3):
+        assert torch.equal(outs_a[l].view(-1), outs_b[l].view(-1))
+        ka, va = ma.pool_tensors(l)
+        kb, vb = mb.pool_tensors(l)
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+        assert ma.get_layer(l).num_cached == mb.get_layer(l).num_cached == cases[l].n_prior + 1
