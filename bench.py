@@ -271,8 +271,10 @@ def run_prefill(args):
     clocks = ClockSampler(0)
     clocks.start()
     t0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -297,6 +299,7 @@ def run_prefill(args):
             "config": {"workload": "config 4: 8192-token prompt in 16 chunks of 512, append + causal attention "
                                    "over all prior pages", "n_q_heads": hq, "n_kv_heads": hkv, "head_dim": d},
             "gpu_launches": 2 * n_chunks * args.steps,
+            "host_enqueue_ms_per_step": round(host_ms, 4),
             "roofline": {"bound": "tensor", "achieved": round(last_flops / (last / 1e3) / 1e12, 2), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(last_flops / (last / 1e3) / 1e12 / peak, 4),
                          "traffic": None, "peak_source": src,

@@ -81,17 +81,24 @@ constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
 __device__ long long g_probe_pf[2 * 128 * 16];
 __device__ long long g_probe_mma[128 * 4];
 __device__ long long g_probe_ld[128 * 8];
+__device__ unsigned long long g_probe_ee[1024 * 4];  // per CTA: entry, setup done, first S ready, exit
+#define PROBE_EE(k)                                                                                          \
+    if (tid == 0) {                                                                                          \
+        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;                      \
+        if (cta < 1024) g_probe_ee[cta * 4 + (k)] = global_timer_ns();                                      \
+    }
 #define PROBE_LD(k)                                                                                  \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 128) g_probe_ld[j * 8 + (k)] = clock64();
+    if (blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 1 && j < 128) g_probe_ld[j * 8 + (k)] = clock64();
 #define PROBE_MMA(k)                                                                                 \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 128) g_probe_mma[j * 4 + (k)] = clock64();
+    if (blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 1 && j < 128) g_probe_mma[j * 4 + (k)] = clock64();
 #define PROBE_PF(k)                                                                                  \
-    if ((tid & 127) == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 128)        \
+    if ((tid & 127) == 0 && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 1 && j < 128) \
         g_probe_pf[((tid >> 7) * 128 + j) * 16 + (k)] = clock64();
 #else
 #define PROBE_PF(k)
 #define PROBE_MMA(k)
 #define PROBE_LD(k)
+#define PROBE_EE(k)
 #endif
 
 // How a tile's 8 pages are copied: 0 = page by page; 1 = one run of
@@ -166,6 +173,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int j0 = rank * n_tiles_all / n_split;
     const int n_tiles = (rank + 1) * n_tiles_all / n_split - j0;
 
+    PROBE_EE(0);
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
@@ -177,6 +185,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    PROBE_EE(1);
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
     const uint32_t t_o = tmem + lane_base + kColO;           // this warp's lanes of O
@@ -409,6 +418,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     float s[64];
     auto load_s = [&](int j) {
         wait(&bar_s[j & 1], (j >> 1) & 1);
+        if (j == 0) { PROBE_EE(2); }
         tc::fence_after_sync();
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -609,22 +619,53 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
     }
     const float inv = 1.f / l_fin;
-    const int q = q0 + r;
-    if (rank == 0 && ok && q < S) {
-        const size_t base = ((size_t)hq * S + q) * kHeadDim + hc * 64;
-        if (a.out_dtype == 0) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
+    // Output tile [128 queries][128 dims] through shared memory (the V stage
+    // buffers, idle now and clear of the merge's receive area), then stored
+    // with consecutive threads on consecutive 16-byte pieces of a row: each
+    // thread alone holds 64 elements of one row, and rows are 256 or 512
+    // bytes apart, so direct stores would touch a new line per lane.
+    if (rank == 0) {
+        const int es = a.out_dtype == 0 ? 4 : 2;
+        uint8_t* stile = smem + kOffV;
+        uint8_t* mine = stile + r * kHeadDim * es + hc * 64 * es;
+        if (es == 4) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-                dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+                reinterpret_cast<float4*>(mine)[i] =
+                    make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
         } else {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) store_out(a.out, base + i, o[i] * inv, a.out_dtype);
+            for (int i = 0; i < 8; ++i) {
+                uint32_t w[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float v0 = o[8 * i + 2 * k] * inv, v1 = o[8 * i + 2 * k + 1] * inv;
+                    uint32_t b0, b1;
+                    if (a.out_dtype == 30) {
+                        b0 = bf16_bits_ref(v0);
+                        b1 = bf16_bits_ref(v1);
+                    } else {
+                        b0 = __half_as_ushort(__float2half_rn(v0));
+                        b1 = __half_as_ushort(__float2half_rn(v1));
+                    }
+                    w[k] = b0 | (b1 << 16);
+                }
+                reinterpret_cast<uint4*>(mine)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        consumer_sync();
+        const int row_chunks = kHeadDim * es / 16;  // 16-byte pieces per row
+        const int rows = min(kBM, S - q0);
+        uint8_t* gout = static_cast<uint8_t*>(a.out) + ((size_t)hq * S + q0) * kHeadDim * es;
+        if (ok) {
+            for (int c = tid; c < rows * row_chunks; c += kConsumerThreads)
+                reinterpret_cast<uint4*>(gout)[c] = reinterpret_cast<const uint4*>(stile)[c];
         }
     }
     if (!ok) atomicOr(a.err, kErrTimeout);
     tc::fence_before_sync();
     __syncthreads();
+    PROBE_EE(3);
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
@@ -685,6 +726,9 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
 #ifdef GKV_PROBE_TIMELINE
 extern "C" int gkv_probe_read_prefill(long long* out, int n) {
     return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_pf, sizeof(long long) * n);
+}
+extern "C" int gkv_probe_read_prefill_ee(unsigned long long* out, int n) {
+    return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_ee, sizeof(unsigned long long) * n);
 }
 extern "C" int gkv_probe_read_prefill_ld(long long* out, int n) {
     return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_ld, sizeof(long long) * n);
