@@ -141,15 +141,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     PROBE_T(0);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    if (a.qk_on && threadIdx.x < 16) {
-        // The QK-norm weights and this position's RoPE rows are not the
-        // previous kernel's outputs: pull them toward L2 before this CTA's
-        // page stream starts, so that the loads after griddepcontrol.wait do
-        // not queue behind it.
-        const size_t pos = (size_t)a.n_prior * kHeadDim;
-        const float* src = lane < 4 ? a.qk.cos + pos : lane < 8 ? a.qk.sin + pos : lane < 12 ? a.qk.q_w : a.qk.k_w;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + (lane & 3) * 32));
-    }
     const int split = blockIdx.x;
     const int Hkv = a.n_kv_heads;
     const int G = a.group;
@@ -237,6 +228,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         // This launch may overlap the tail of the previous kernel on the stream
         // (programmatic dependent launch): the page stream above reads only
         // cached pages, but Q and the new K/V row are that kernel's outputs.
+        // QK-norm weights and this position's RoPE rows are not the previous
+        // kernel's outputs: they are loaded before the wait, whose latency
+        // covers theirs.
+        RowParamsG8 rq;
+        if (a.qk_on) {
+            const size_t pos = (size_t)a.n_prior * kHeadDim;
+            rq = load_row_params_g8(a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, lane & 7);
+        }
         asm volatile("griddepcontrol.wait;" ::: "memory");
         PROBE_T(5);
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
@@ -268,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                         for (int k = 0; k < 4; ++k)
                             x[it][k] = __uint_as_float((uint32_t)qr[32 * it + 8 * k + j] << 16);
                     uint16_t o[4][4];
-                    norm_rope_row_g8(x, j, a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, a.qk.eps, o);
+                    norm_rope_row_g8(x, j, rq, a.qk.eps, o);
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {  // groups 2 half, 2 half + 1 -> staging rows 0, 1
                         if ((grp >> 1) == half && row_ok) {

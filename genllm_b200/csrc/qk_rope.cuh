@@ -74,8 +74,29 @@ __device__ __forceinline__ void norm_rope_row(const float (&x)[4], const RowPara
 // 0..3): the AVX2 accumulator (k, j) is then a chain inside one lane, and the
 // RoPE pairs (e, e + 64) are (it, it + 2) of the same lane. x/out indexed
 // [it][k]; w/cs/sn are the full rows (weights, the position's cos/sin).
-__device__ __forceinline__ void norm_rope_row_g8(const float (&x)[4][4], int j, const float* w, const float* cs,
-                                                 const float* sn, float eps, uint16_t (&out)[4][4]) {
+// This lane's parameters for norm_rope_row_g8: the weights of its 16
+// elements and the cos/sin of its 8 RoPE pairs at the row's position.
+struct RowParamsG8 {
+    float w[4][4], c[2][4], s[2][4];
+};
+__device__ __forceinline__ RowParamsG8 load_row_params_g8(const float* w, const float* cs, const float* sn, int j) {
+    RowParamsG8 p;
+#pragma unroll
+    for (int it = 0; it < 4; ++it)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) p.w[it][k] = w[32 * it + 8 * k + j];
+#pragma unroll
+    for (int it = 0; it < 2; ++it)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            p.c[it][k] = cs[32 * it + 8 * k + j];
+            p.s[it][k] = sn[32 * it + 8 * k + j];
+        }
+    return p;
+}
+
+__device__ __forceinline__ void norm_rope_row_g8(const float (&x)[4][4], int j, const RowParamsG8& p, float eps,
+                                                 uint16_t (&out)[4][4]) {
     float acc[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -94,15 +115,14 @@ __device__ __forceinline__ void norm_rope_row_g8(const float (&x)[4][4], int j, 
     for (int it = 0; it < 4; ++it)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const float v = __fmul_rn(__fmul_rn(x[it][k], rms), w[32 * it + 8 * k + j]);
+            const float v = __fmul_rn(__fmul_rn(x[it][k], rms), p.w[it][k]);
             y[it][k] = __uint_as_float(__float_as_uint(v) & 0xFFFF0000u);
         }
 #pragma unroll
     for (int it = 0; it < 2; ++it)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int e = 32 * it + 8 * k + j;
-            const float c = cs[e], s = sn[e];
+            const float c = p.c[it][k], s = p.s[it][k];
             out[it][k] = bf16_bits_ref(__fmaf_rn(y[it][k], c, -__fmul_rn(y[it + 2][k], s)));
             out[it + 2][k] = bf16_bits_ref(__fmaf_rn(y[it][k], s, __fmul_rn(y[it + 2][k], c)));
         }
