@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--pool", type=int, default=0, help="pages per pool (0: max(4096, ctx/16 + 64))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qknorm"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qknorm", "flash"],
                     help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor "
                          "cores; qknorm: config 3 fed the Q/K/V projections, QK-norm + RoPE fused into the step")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
@@ -309,6 +309,56 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+def run_flash(args):
+    """The reference's non-paged attention op (FlashAttentionImpl) on the
+    tcgen05 kernel: one causal self-attention call over an 8192-token
+    sequence, Qwen3-1.7B layer shape (Hq 16, Hkv 8, D 128, bf16). Metric:
+    causal-exact TFLOP/s (4 * D * Hq * sum of visible keys)."""
+    import torch
+    from genllm_b200.paged_attention import flash_attention
+
+    torch.cuda.set_device(0)
+    B, hq, hkv, d, S = 1, 16, 8, 128, 8192
+    g = torch.Generator(device="cuda").manual_seed(9)
+    Q = torch.randn(B, hq, S, d, generator=g, device="cuda").to(torch.bfloat16)
+    K = torch.randn(B, hkv, S, d, generator=g, device="cuda").to(torch.bfloat16)
+    V = torch.randn(B, hkv, S, d, generator=g, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(Q)
+    for _ in range(args.warmup):
+        flash_attention(Q, K, V, out=out)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0.record(stream)
+    for _ in range(args.steps):
+        flash_attention(Q, K, V, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = 4.0 * d * hq * B * sum(p + 1 for p in range(S))
+    tf = flops / (ms / 1e3) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        peak, src = 1590.0, "fallback 1.59 PFLOP/s"
+    line = {"metric": "non-paged causal attention TFLOP/s (causal-exact), Qwen3-1.7B layer shape, 8192 tokens",
+            "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "FlashAttentionImpl: one self-attention call, B 1, S 8192, causal",
+                       "n_q_heads": hq, "n_kv_heads": hkv, "head_dim": d},
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "traffic": None, "peak_source": src,
+                         "kernel": "prefill_tc_kernel (contiguous K/V)"},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def run_qknorm(args):
     """Config 3 on the projections: each layer-token's Q/K/V arrive as the
     Q/K/V projections ([1, H*128] bf16) and go through QK-norm + RoPE before
@@ -444,6 +494,9 @@ def main():
         return
     if args.workload == "qknorm":
         run_qknorm(args)
+        return
+    if args.workload == "flash":
+        run_flash(args)
         return
 
     import torch

@@ -92,6 +92,8 @@ SIGNATURES = {
     "gkv_paged_decode_static_scratch": ([C.POINTER(PoolDesc), vp, i32, vp, vp, vp, vp, i32, C.c_float, i32, vp],
                                         C.c_int),
     "gkv_rope_cache": ([C.c_float, i32, i32, vp, vp], C.c_int),
+    "gkv_flash_attention": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, C.c_float, i32, i32, i32, vp], C.c_int),
+    "gkv_flash_check_errors": ([u32p], C.c_int),
     "gkv_decode_layers": ([vp, i32, i32p, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), i32, C.c_float,
                            i32, vp], C.c_int),
     "gkv_qk_norm_rope": ([vp, vp, vp, i32, i32, i32, C.POINTER(QkNormDesc), i32, vp, vp, vp, vp], C.c_int),

@@ -142,6 +142,15 @@ bool encode_pool_run_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtens
            encode(v_map, pool.v_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
 }
 
+bool encode_contig_kv_maps_sw128(const uint16_t* k, const uint16_t* v, int32_t rows_per_head, int32_t heads,
+                                 CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows_per_head, (cuuint64_t)heads};
+    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)rows_per_head * kHeadDim * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    return encode(k_map, const_cast<uint16_t*>(k), 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why) &&
+           encode(v_map, const_cast<uint16_t*>(v), 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
+}
+
 bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, CUtensorMap* q_map,
                         const char** why) {
     cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)seq_len, (cuuint64_t)n_q_heads};

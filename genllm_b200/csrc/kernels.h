@@ -137,6 +137,26 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
                               const int2* table, const PrefillLaunch& p, uint32_t* err,
                               int num_sms, cudaStream_t stream);
 
+// Non-paged attention (the reference's FlashAttentionImpl): B sequences of
+// seq_len tokens, Q [B][Hq][S][128], K/V [B][Hkv][S][128] contiguous,
+// self-attention (query s at position s), on the same tcgen05 kernel with the
+// K/V tiles copied straight from the tensors.
+struct FlashLaunch {
+    void* out;          // [B][Hq][S][128]
+    int32_t out_dtype;
+    int32_t batch;
+    int32_t n_q_heads;
+    int32_t n_kv_heads;
+    int32_t seq_len;
+    float scale;
+    int32_t causal;
+};
+// K/V tensor maps over [B*Hkv][S][128], box {64, 128, 1}, 128-byte swizzle.
+bool encode_contig_kv_maps_sw128(const uint16_t* k, const uint16_t* v, int32_t rows_per_head, int32_t heads,
+                                 CUtensorMap* k_map, CUtensorMap* v_map, const char** why);
+cudaError_t launch_flash_tc(const CUtensorMap& q_map, const CUtensorMap& k_map, const CUtensorMap& v_map,
+                            const FlashLaunch& f, uint32_t* err, int num_sms, cudaStream_t stream);
+
 // The same on CUDA cores (one warp per query row); kept as an independent
 // second implementation for cross-checking.
 cudaError_t launch_prefill_simt(const PoolView& pool, const int2* table, const PrefillLaunch& p,

@@ -65,8 +65,9 @@ struct TcParams {
     int32_t n_pages;
     int32_t pool_pages;
     int32_t causal;
-    int32_t runs;  // k_run / v_run maps usable
-    float qscale;  // softmax scale * log2(e)
+    int32_t runs;    // k_run / v_run maps usable
+    int32_t contig;  // 1: K/V are contiguous [B*Hkv][S][128] (k_run / v_run map them), no table
+    float qscale;    // softmax scale * log2(e)
 };
 
 constexpr int kConsumerThreads = 256;               // 8 warps: 2 threads per query row
@@ -161,7 +162,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int q0 = blockIdx.x * kBM;
     const int hq = blockIdx.y;
     const int G = a.n_q_heads / a.n_kv_heads;
-    const int h = hq / G;
+    // Paged: blockIdx.y is the query head. Contiguous (non-paged attention
+    // over B sequences): blockIdx.y = b * Hq + head, and the K/V rows of
+    // (b, kv head) sit at index b * Hkv + head / G of the tensor map.
+    const int h = a.contig ? (hq / a.n_q_heads) * a.n_kv_heads + (hq % a.n_q_heads) / G : hq / G;
     const int S = a.seq_len;
     const int first_q_abs = a.total - S + q0;
     const int last_q_abs = min(a.total - 1, first_q_abs + kBM - 1);
@@ -218,6 +222,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         const int st = j % kStages;
         uint64_t* bar = which ? &bar_v[st] : &bar_k[st];
         mbar_arrive_expect_tx(bar, kTile);
+        if (a.contig) {  // 128 consecutive key rows (past S: zero-filled by the copy)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+                tma_load_3d(smem + (which ? kOffV : kOffK) + st * kTile + hf * kHalf, which ? &v_run : &k_run, bar,
+                            hf * 64, (j0 + j) * kBN, h, pol_kv);
+            return;
+        }
         const int mode = tile_mode_regs(ids, a.pool_pages, a.runs);
         if (mode != 0) {
             const int first = which ? ids[0].y : ids[0].x;
@@ -353,9 +364,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
             uint64_t* freed = which ? bar_vfree : bar_kfree;
             int2 ids[kPagesPerTile], nxt[kPagesPerTile];
-            if (n_tiles > 0) load_ids(0, ids);
+            if (n_tiles > 0 && !a.contig) load_ids(0, ids);
             for (int j = 0; j < n_tiles && ok; ++j) {
-                if (j + 1 < n_tiles) load_ids(j + 1, nxt);
+                if (j + 1 < n_tiles && !a.contig) load_ids(j + 1, nxt);
                 if (which == 0) { PROBE_LD(0); }
                 if (j >= kStages) wait(&freed[j % kStages], (j / kStages - 1) & 1);
                 if (which == 0) { PROBE_LD(1); }
@@ -407,6 +418,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     // (fetched a tile ahead) to derive its copy mode.
     const int lane = tid & 31;
     auto entry = [&](int j) {
+        if (a.contig) return make_int2(-1, -1);  // no table: every tile is in key order (mode 0)
         int lp = (j0 + j) * kPagesPerTile + (lane & (kPagesPerTile - 1));
         if (lp >= a.n_pages) lp = a.n_pages - 1;
         return a.table[lp];
@@ -674,9 +686,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
 }  // namespace
 
-cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const PoolMaps& maps,
-                              const int2* table, const PrefillLaunch& p, uint32_t* err, int num_sms,
-                              cudaStream_t stream) {
+namespace {
+// Launch prefill_tc_kernel over `rows` query rows of `heads` (query heads, or
+// sequences x query heads), splitting the KV range over a cluster of up to 3
+// CTAs while the query tiles alone would leave SMs idle.
+cudaError_t launch_tc(const CUtensorMap& q_map, const PoolMaps& maps, const TcParams& a, int rows, int heads,
+                      int num_sms, cudaStream_t stream) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -686,6 +701,29 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
+    const int tiles = ((rows + kBM - 1) / kBM) * heads;
+    int n_split = num_sms / (tiles > 0 ? tiles : 1);
+    if (n_split > 3) n_split = 3;
+    if (n_split < 1) n_split = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows + kBM - 1) / kBM, heads, n_split);
+    cfg.blockDim = dim3(kThreadsTc);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = n_split;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, maps.k, maps.v, maps.k_run, maps.v_run, a);
+}
+}  // namespace
+
+cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, const PoolMaps& maps,
+                              const int2* table, const PrefillLaunch& p, uint32_t* err, int num_sms,
+                              cudaStream_t stream) {
     TcParams a;
     a.table = table;
     a.out = p.out;
@@ -699,26 +737,30 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
     a.pool_pages = pool.pool_pages;
     a.causal = p.causal;
     a.runs = maps.runs ? 1 : 0;
+    a.contig = 0;
     a.qscale = p.scale * 1.4426950408889634f;
-    // Split the KV range over a cluster of up to 3 CTAs while the query tiles
-    // alone would leave SMs idle.
-    const int tiles = ((p.seq_len + kBM - 1) / kBM) * p.n_q_heads;
-    int n_split = num_sms / (tiles > 0 ? tiles : 1);
-    if (n_split > 3) n_split = 3;
-    if (n_split < 1) n_split = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.seq_len + kBM - 1) / kBM, p.n_q_heads, n_split);
-    cfg.blockDim = dim3(kThreadsTc);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = n_split;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, maps.k, maps.v, maps.k_run, maps.v_run, a);
+    return launch_tc(q_map, maps, a, p.seq_len, p.n_q_heads, num_sms, stream);
+}
+
+cudaError_t launch_flash_tc(const CUtensorMap& q_map, const CUtensorMap& k_map, const CUtensorMap& v_map,
+                            const FlashLaunch& f, uint32_t* err, int num_sms, cudaStream_t stream) {
+    TcParams a;
+    a.table = nullptr;
+    a.out = f.out;
+    a.err = err;
+    a.out_dtype = f.out_dtype;
+    a.n_q_heads = f.n_q_heads;
+    a.n_kv_heads = f.n_kv_heads;
+    a.seq_len = f.seq_len;
+    a.total = f.seq_len;  // self-attention over the chunk: query s sits at position s
+    a.n_pages = 0;
+    a.pool_pages = 0;
+    a.causal = f.causal;
+    a.runs = 0;
+    a.contig = 1;
+    a.qscale = f.scale * 1.4426950408889634f;
+    const PoolMaps maps{k_map, v_map, k_map, v_map, false};
+    return launch_tc(q_map, maps, a, f.seq_len, f.batch * f.n_q_heads, num_sms, stream);
 }
 
 }  // namespace gkv

@@ -357,3 +357,33 @@ class DecodeStep:
         check(lib().gkv_decode_layers(self.manager.handle, self._n, self._ids, self._q, self._k, self._v, self._o,
                                       self._hq, self._scale, self._odt, _stream_handle(self.manager.device, stream)))
 
+
+def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, out: Optional[torch.Tensor] = None,
+                    scale: Optional[float] = None, causal: bool = True, stream=None) -> torch.Tensor:
+    """``FlashAttentionImpl<CUDA>::execute`` on torch tensors: Q [B, Hq, S, D],
+    K/V [B, Hkv, S, D] bf16 contiguous (self-attention over each sequence);
+    out [B, Hq, S, D] (Q's dtype by default). gkv_flash_attention."""
+    if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
+        raise GkvError(_lib.GKV_ERR_INVALID, "Q, K, V must be [B, H, S, D]")
+    B, Hq, S, D = Q.shape
+    if out is None:
+        out = torch.empty_like(Q)
+    sc = float(scale) if scale is not None else 1.0 / float(D) ** 0.5
+    for t in (Q, K, V, out):
+        if not t.is_contiguous() or t.device != Q.device:
+            raise GkvError(_lib.GKV_ERR_INVALID, "tensors must be contiguous and on one device")
+    check(lib().gkv_flash_attention(C.c_void_p(Q.data_ptr()), C.c_void_p(K.data_ptr()), C.c_void_p(V.data_ptr()),
+                                    C.c_void_p(out.data_ptr()), B, Hq, K.shape[1], S, D, sc, 1 if causal else 0,
+                                    _TORCH_TO_GKV[Q.dtype], _TORCH_TO_GKV[out.dtype],
+                                    _stream_handle(Q.device, stream)))
+    return out
+
+
+def flash_check_errors() -> int:
+    """The current device's flash-attention error word (read and cleared)."""
+    v = C.c_uint32(0)
+    st = lib().gkv_flash_check_errors(C.byref(v))
+    if st not in (0, _lib.GKV_ERR_DEVICE):
+        check(st)
+    return v.value
+

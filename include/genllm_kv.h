@@ -355,6 +355,21 @@ int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_f
                                const void* v_flat, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
                                int32_t causal, int32_t out_dtype, const gkv_qk_norm* qk, gkv_stream_t stream);
 
+/* ---------------- non-paged attention ------------------------------------
+ * FlashAttentionImpl<CUDA>::execute (src/backend/cuda/attention.cu:317-399;
+ * semantics of the CPU op, src/backend/cpu/attention.cpp:39-120):
+ * self-attention of `batch` sequences of seq_len tokens each, Q
+ * [B][Hq][S][D], K/V [B][Hkv][S][D] contiguous device tensors, query s at
+ * position s (causal: keys 0..s), GQA group Hq / Hkv, out [B][Hq][S][D] in
+ * out_dtype. Runs on the tcgen05 chunked-prefill kernel with its K/V tiles
+ * copied straight from the tensors. head_dim 128, bf16. Allocates nothing;
+ * timeouts set the current device's error word, read (and cleared) by
+ * gkv_flash_check_errors (GKV_ERR_DEVICE when set). */
+int gkv_flash_attention(const void* Q, const void* K, const void* V, void* out, int32_t batch, int32_t n_q_heads,
+                        int32_t n_kv_heads, int32_t seq_len, int32_t head_dim, float scale, int32_t causal,
+                        int32_t dtype, int32_t out_dtype, gkv_stream_t stream);
+int gkv_flash_check_errors(uint32_t* flags);
+
 #ifdef __cplusplus
 }
 #endif

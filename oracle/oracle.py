@@ -82,6 +82,8 @@ class Oracle:
         L.orc_apply_rope_bf16.restype = None
         L.orc_rope_cache.argtypes = [C.c_float, C.c_int32, C.c_int32, _vp, _vp]
         L.orc_rope_cache.restype = None
+        L.orc_flash_attention_f32.argtypes = [_vp, _vp, _vp] + [C.c_int32] * 6 + [C.c_float, C.c_int, _vp]
+        L.orc_flash_attention_f32.restype = None
 
     def paged_attention_f32(self, q, k_pool, v_pool, k_ids, v_ids, total, n_q_heads, n_kv_heads,
                             seq_len, head_dim, scale, causal=True, dtype=BF16, threads=0):
@@ -143,6 +145,17 @@ class Oracle:
         sin = np.empty((max_seq, head_dim), dtype=np.float32)
         self.lib.orc_rope_cache(theta, head_dim, max_seq, _ptr(cos), _ptr(sin))
         return cos, sin
+
+    def flash_attention_f32(self, q, k, v, scale, causal=True):
+        """q uint16 [B][Hq][S][D], k/v [B][Hkv][S][D] -> fp32 [B][Hq][S][D]
+        (flash_oracle.c)."""
+        q, k, v = (np.ascontiguousarray(a, dtype=np.uint16) for a in (q, k, v))
+        B, Hq, S, D = q.shape
+        Hkv = k.shape[1]
+        out = np.empty((B, Hq, S, D), dtype=np.float32)
+        self.lib.orc_flash_attention_f32(_ptr(q), _ptr(k), _ptr(v), B, Hq, Hkv, S, D, Hq // Hkv, scale,
+                                         int(bool(causal)), _ptr(out))
+        return out
 
 
 class OraclePool:
@@ -307,6 +320,7 @@ class RefSession:
                                          C.c_float, C.c_int32], None),
                 "ref_paged_attention_layers": ([_vp, C.c_int32, _vp, _vp, _vp, _vp, C.c_int32,
                                                 C.c_int32, C.c_float, C.c_int32], None),
+                "ref_flash_attention": ([_vp, _vp, _vp, _vp] + [C.c_int32] * 5 + [C.c_float, C.c_int32], None),
             }
             for k, (a, r) in sig.items():
                 getattr(L, k).argtypes = a
@@ -435,3 +449,14 @@ def run_ref_case(case, causal=True):
         return out, ref.pool_view(0, 0).copy(), ref.pool_view(0, 1).copy(), k_ids, v_ids, nc
     finally:
         ref.close()
+
+
+def ref_flash_attention(q, k, v, scale, causal=True):
+    """The reference's FlashAttentionImpl<CPU> (oracle/_ref): bf16 out bits."""
+    L = RefSession.lib()
+    q, k, v = (np.ascontiguousarray(a, dtype=np.uint16) for a in (q, k, v))
+    B, Hq, S, D = q.shape
+    out = np.empty_like(q)
+    L.ref_flash_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, Hq, k.shape[1], S, D, scale, int(bool(causal)))
+    return out
+

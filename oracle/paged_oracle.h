@@ -110,6 +110,12 @@ void orc_apply_rope_bf16(const uint16_t* x, uint16_t* out, const float* cos_tab,
                          int64_t n_heads, int64_t seq, int64_t head_dim, int64_t start_pos);
 void orc_rope_cache(float theta, int32_t head_dim, int32_t max_seq, float* cos_out, float* sin_out);
 
+/* flash_oracle.c: the non-paged attention op (self-attention over one chunk),
+ * q [B][Hq][S][D], k/v [B][Hkv][S][D] bf16; out [B][Hq][S][D] fp32. */
+void orc_flash_attention_f32(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch, int32_t Hq,
+                             int32_t Hkv, int32_t S, int32_t D, int32_t groups, float scale, int causal,
+                             float* out);
+
 /* Round an fp32 buffer to the reference's bf16 (RNE, subnormals to signed 0). */
 void orc_round_bf16(const float* in, uint16_t* out, size_t n);
 

@@ -155,4 +155,22 @@ void ref_paged_attention_layers(void* h, int32_t n_layers, void** Q, void** K, v
     for (auto& t : th) t.join();
 }
 
+// One call of ops::FlashAttentionImpl<Device::CPU>::execute
+// (src/backend/cpu/attention.cpp:39-120): Q [B][Hq][S][D], K/V [B][Hkv][S][D]
+// bf16; out [B][Hq][S][D] bf16, as the reference writes it.
+void ref_flash_attention(const void* Q, const void* K, const void* V, void* out, int32_t batch, int32_t n_q_heads,
+                         int32_t n_kv_heads, int32_t seq_len, int32_t head_dim, float scale, int32_t causal) {
+    Tensor q, k, v, o;
+    q.data = const_cast<void*>(Q); k.data = const_cast<void*>(K); v.data = const_cast<void*>(V); o.data = out;
+    for (Tensor* t : {&q, &k, &v, &o}) { t->device = Device::CPU; t->dtype = DataType::GGML_TYPE_BF16; }
+    q.dims = {batch, n_q_heads, seq_len, head_dim};
+    k.dims = {batch, n_kv_heads, seq_len, head_dim};
+    v.dims = k.dims;
+    o.dims = q.dims;
+    o.src[0] = &q; o.src[1] = &k; o.src[2] = &v;
+    o.op_params = {static_cast<float>(head_dim), scale, static_cast<float>(causal),
+                   static_cast<float>(n_q_heads / n_kv_heads)};
+    ops::FlashAttentionImpl<Device::CPU>::execute(&o, 0);
+}
+
 }  // extern "C"

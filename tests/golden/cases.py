@@ -28,3 +28,10 @@ QK_ROPE = [
     ("qkrope_from_zero", dict(seed=33, n_q_heads=4, n_kv_heads=2, seq_len=20, start_pos=0), 64),
 ]
 
+# Non-paged attention (FlashAttentionImpl<CPU>): (name, seed, B, Hq, Hkv, S,
+# causal). Fixtures hold the reference's bf16 output and the inputs' checksums.
+FLASH = [
+    ("flash_b2_causal", 41, 2, 8, 2, 37, True),
+    ("flash_b1_noncausal", 42, 1, 4, 4, 20, False),
+]
+

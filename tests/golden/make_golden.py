@@ -18,9 +18,9 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, HERE)
 
-from cases import CONFIG1, QK_ROPE, SMALL  # noqa: E402
+from cases import CONFIG1, FLASH, QK_ROPE, SMALL  # noqa: E402
 from genllm_b200.synth import fragmented_case, heads_major, qk_rope_case  # noqa: E402
-from oracle.oracle import RefOps, run_ref_case  # noqa: E402
+from oracle.oracle import RefOps, ref_flash_attention, run_ref_case  # noqa: E402
 
 
 def sha(a: np.ndarray) -> str:
@@ -46,6 +46,23 @@ def main():
                         pools_after_sha=np.array([sha(kp), sha(vp)]))
     print(name, out.shape, nc)
     make_qk_rope()
+    make_flash()
+
+
+def flash_inputs(seed, B, Hq, Hkv, S):
+    from genllm_b200.synth import randn_bf16
+    rng = np.random.default_rng(seed)
+    return (randn_bf16(rng, (B, Hq, S, 128)), randn_bf16(rng, (B, Hkv, S, 128)), randn_bf16(rng, (B, Hkv, S, 128)))
+
+
+def make_flash():
+    """FlashAttentionImpl<CPU> (src/backend/cpu/attention.cpp:39-120)."""
+    for name, seed, B, Hq, Hkv, S, causal in FLASH:
+        q, k, v = flash_inputs(seed, B, Hq, Hkv, S)
+        out = ref_flash_attention(q, k, v, float(1 / np.sqrt(128)), causal)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), out_bf16=out,
+                            inputs_sha=np.array([sha(q), sha(k), sha(v)]))
+        print(name, out.shape)
 
 
 def make_qk_rope():
