@@ -625,7 +625,11 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     }
     if (!gather) return;
     // ---- fused head all-gather: completion protocol ----
-    __threadfence_system();  // this CTA's peer stores are visible before its ticket
+    // This CTA's peer stores are ordered before its ticket at GPU scope; the
+    // last CTA's system-scope fence and release (cumulative over what it
+    // observed through the tickets) publish every CTA's stores to the peers.
+    // A system-scope fence in every CTA cost ~9 us per layer at 2 GPUs.
+    __threadfence();
     __syncthreads();
     __shared__ uint32_t s_last;
     if (threadIdx.x == 0) {
