@@ -643,9 +643,12 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     }
     if (threadIdx.x == 0) {
         *c.g.ticket = 0u;
+        // One system-scope fence, then plain (relaxed) flag stores: together
+        // a release of every block this rank stored. A release store per
+        // flag would put a system-scope fence in front of each of them.
         __threadfence_system();
         for (int r = 0; r < c.g.world; ++r)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(c.g.flag_dst[r]), "r"(c.g.epoch) : "memory");
+            asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(c.g.flag_dst[r]), "r"(c.g.epoch) : "memory");
     }
     __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
