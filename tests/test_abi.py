@@ -34,3 +34,20 @@ def test_status_strings():
     L = _lib.lib()
     assert L.gkv_status_string(0) == b"ok"
     assert L.gkv_status_string(2) == b"page pool exhausted"
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_gpu():
+    """Argument checks come before any CUDA call: they answer on a host
+    without a GPU too."""
+    import ctypes as C
+    from genllm_b200 import _lib
+    L = _lib.lib()
+    assert L.gkv_flash_attention(None, None, None, None, 1, 8, 8, 16, 128, 0.1, 1, 30, 30, None) == _lib.GKV_ERR_INVALID
+    assert L.gkv_qk_norm_rope(None, None, None, 1, 8, 8, None, 0, None, None, None, None) == _lib.GKV_ERR_INVALID
+    assert L.gkv_decode_layers(None, 0, None, None, None, None, None, 8, 0.1, 30, None) == _lib.GKV_ERR_INVALID
+    assert L.gkv_rope_cache(1e6, 127, 4, None, None) == _lib.GKV_ERR_INVALID
+    import numpy as np
+    c = np.zeros((4, 128), np.float32)
+    s = np.zeros((4, 128), np.float32)
+    assert L.gkv_rope_cache(1e6, 128, 4, C.c_void_p(c.ctypes.data), C.c_void_p(s.ctypes.data)) == 0
+    assert c[0, 0] == 1.0 and s[0, 0] == 0.0

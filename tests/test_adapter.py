@@ -12,8 +12,9 @@ REF = "/root/reference"
 
 
 @pytest.mark.skipif(not os.path.isdir(REF) or not shutil.which("g++"), reason="reference tree absent")
-def test_adapter_compiles_against_reference_headers():
-    src = os.path.join(ROOT, "genllm_b200", "adapter", "paged_attention_cuda.cpp")
+@pytest.mark.parametrize("name", ["paged_attention_cuda.cpp", "flash_attention_cuda.cpp"])
+def test_adapter_compiles_against_reference_headers(name):
+    src = os.path.join(ROOT, "genllm_b200", "adapter", name)
     cmd = ["g++", "-std=c++23", "-fsyntax-only", "-DBACKEND_CUDA", "-I", os.path.join(ROOT, "oracle", "polyfill"),
            "-I", os.path.join(ROOT, "include"), "-I", f"{REF}/include", "-I", f"{REF}/include/utils",
            "-I", f"{REF}/include/core", "-I", f"{REF}/include/3rd", "-I", "/usr/local/cuda/include", src]
