@@ -181,6 +181,16 @@ struct gkv_table {
     bool runs = false;      // run maps valid (the pool holds at least 8 pages)
     void* qk_buf = nullptr;  // normalised / rotated / permuted Q, K, V of a chunk (gkv_paged_attention_raw_qknorm)
     size_t qk_bytes = 0;
+    // Q tensor maps of recent chunk calls, keyed by (pointer, heads, rows):
+    // an executor reuses its activation buffers, and encoding a map is a
+    // driver call on every chunk otherwise.
+    struct QMap {
+        const void* q = nullptr;
+        int32_t heads = 0, rows = 0;
+        CUtensorMap map;
+    };
+    QMap qmaps[16];
+    int qmap_next = 0;
 };
 
 namespace {
@@ -475,12 +485,23 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
     if (prefill_on_cuda_cores()) {
         e = gkv::launch_prefill_simt(pv, t->d_table, pl, t->scratch.err, s);
     } else {
-        CUtensorMap q_map;
-        const char* why = nullptr;
-        if (!gkv::encode_q_map_sw128(pl.q, n_q_heads, seq_len, &q_map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
+        const CUtensorMap* q_map = nullptr;
+        for (const auto& e : t->qmaps)
+            if (e.q == pl.q && e.heads == n_q_heads && e.rows == seq_len) q_map = &e.map;
+        if (!q_map) {
+            auto& e = t->qmaps[t->qmap_next];
+            t->qmap_next = (t->qmap_next + 1) % 16;
+            const char* why = nullptr;
+            e.q = nullptr;
+            if (!gkv::encode_q_map_sw128(pl.q, n_q_heads, seq_len, &e.map, &why)) return fail(GKV_ERR_CUDA, "%s", why);
+            e.q = pl.q;
+            e.heads = n_q_heads;
+            e.rows = seq_len;
+            q_map = &e.map;
+        }
         const gkv::PoolMaps maps{t->k_map_sw, t->v_map_sw, t->runs ? t->k_map_run : t->k_map_sw,
                                  t->runs ? t->v_map_run : t->v_map_sw, t->runs};
-        e = gkv::launch_prefill_tc(pv, q_map, maps, t->d_table, pl, t->scratch.err, t->num_sms, s);
+        e = gkv::launch_prefill_tc(pv, *q_map, maps, t->d_table, pl, t->scratch.err, t->num_sms, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
     return GKV_OK;
