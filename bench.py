@@ -49,9 +49,10 @@ def parse():
     ap.add_argument("--pool", type=int, default=0, help="pages per pool (0: max(4096, ctx/16 + 64))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qknorm", "flash"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qknorm", "flash", "export"],
                     help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor "
-                         "cores; qknorm: config 3 fed the Q/K/V projections, QK-norm + RoPE fused into the step")
+                         "cores; qknorm: config 3 fed the Q/K/V projections, QK-norm + RoPE fused into the step; "
+                         "export: config 3's 36 layers exported to head-major e4m3 (KV format row)")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: head all-gather fused into the decode (NVLink peer stores) or NCCL all_gather")
     ap.add_argument("--no-kernel-events", action="store_true",
@@ -359,6 +360,180 @@ def run_flash(args):
     print(json.dumps(line), flush=True)
 
 
+def run_export(args):
+    """KV format export: config 3's cache (36 layers x 32k tokens, Hkv 8, D
+    128, fragmented 4096-page pools) exported to dense head-major e4m3 with
+    per (head, 16-token block) scales -- one kv_export_kernel launch per
+    layer. A step = all 36 layers. Metric: algorithmic HBM GB/s (pages read
+    2 B/element, e4m3 written 1 B/element, scales 4 B per block). Also timed:
+    the bf16 export and the e4m3 import (same bytes in the other direction);
+    e2e = the export plus the device-to-host copy of its output into pinned
+    host memory (a KV offload)."""
+    import torch
+    from genllm_b200.paged_attention import PagedAttentionManager
+
+    torch.cuda.set_device(0)
+    L, n, hkv, pages = args.layers, args.ctx, HKV, pool_pages(args)
+    dev = torch.device("cuda:0")
+    m = PagedAttentionManager(0)
+    g = torch.Generator(device=dev).manual_seed(6)
+    for l in range(L):
+        m.init_layer(l, hkv, D)
+        m.reserve_layer(l, pages)
+        kp, vp = m.pool_tensors(l)
+        kp.copy_(torch.randn(kp.shape, generator=g, device=dev).to(torch.bfloat16))
+        vp.copy_(torch.randn(vp.shape, generator=g, device=dev).to(torch.bfloat16))
+        for w in (0, 1):
+            pool = m.pool(l, w)
+            for _ in range(pages):
+                pool.alloc()
+        pk = torch.randperm(pages, generator=torch.Generator().manual_seed(100 + l))[: (n + 15) // 16]
+        pv = torch.randperm(pages, generator=torch.Generator().manual_seed(200 + l))[: (n + 15) // 16]
+        m.set_page_table(l, pk.tolist(), pv.tolist(), n)
+    nb = (n + 15) // 16
+    elems = 2 * hkv * n * D
+    fp8_bytes = elems * 3 + 2 * hkv * nb * 4       # read bf16, write e4m3 + scales
+    bf16_bytes = elems * 4
+    # preallocated outputs: the export writes into them through the raw C ABI
+    import ctypes as C
+    from genllm_b200 import _lib
+    K8 = [torch.empty((hkv, n, D), dtype=torch.uint8, device=dev) for _ in range(L)]
+    V8 = [torch.empty_like(K8[0]) for _ in range(L)]
+    KS = [torch.empty((hkv, nb), dtype=torch.float32, device=dev) for _ in range(L)]
+    VS = [torch.empty_like(KS[0]) for _ in range(L)]
+    K16 = torch.empty((hkv, n, D), dtype=torch.bfloat16, device=dev)
+    V16 = torch.empty_like(K16)
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+    cnt = C.c_int32()
+
+    def export(l, fmt):
+        if fmt == _lib.GKV_KV_FP8_E4M3:
+            args_ = (K8[l], V8[l], KS[l], VS[l])
+        else:
+            args_ = (K16, V16, None, None)
+        _lib.check(_lib.lib().gkv_export_kv(m.handle, l, fmt, *[C.c_void_p(t.data_ptr() if t is not None else 0)
+                                                                  for t in args_], C.byref(cnt), sh))
+
+    def step(fmt=_lib.GKV_KV_FP8_E4M3, events=None):
+        for l in range(L):
+            if events is not None:
+                events[l][0].record(stream)
+            export(l, fmt)
+            if events is not None:
+                events[l][1].record(stream)
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    # headline: the e4m3 export, per-launch events inside the timed region
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(L)]
+          for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0.record(stream)
+    for k in range(args.steps):
+        step(events=ev[k])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    launch_ms = statistics.mean(a.elapsed_time(b) for e in ev for a, b in e)
+    gbs = fp8_bytes * L / (ms / 1e3) / 1e9
+    ms_bf16 = timed(lambda: step(_lib.GKV_KV_BF16), args.steps)
+
+    # e4m3 import of the exported layers into a second manager (reset per step)
+    m2 = PagedAttentionManager(0)
+    for l in range(L):
+        m2.init_layer(l, hkv, D)
+        m2.reserve_layer(l, pages)
+
+    def import_step():
+        m2.reset()
+        for l in range(L):
+            _lib.check(_lib.lib().gkv_import_kv(m2.handle, l, _lib.GKV_KV_FP8_E4M3, C.c_void_p(K8[l].data_ptr()),
+                                                C.c_void_p(V8[l].data_ptr()), C.c_void_p(KS[l].data_ptr()),
+                                                C.c_void_p(VS[l].data_ptr()), n, sh))
+    ms_import = timed(import_step, args.steps)
+
+    # e2e: export + D2H of every layer's e4m3 output and scales into pinned memory
+    host = [(torch.empty(K8[0].shape, dtype=torch.uint8, pin_memory=True),
+             torch.empty(V8[0].shape, dtype=torch.uint8, pin_memory=True),
+             torch.empty(KS[0].shape, dtype=torch.float32, pin_memory=True),
+             torch.empty(VS[0].shape, dtype=torch.float32, pin_memory=True)) for _ in range(L)]
+
+    def e2e_step():
+        for l in range(L):
+            export(l, _lib.GKV_KV_FP8_E4M3)
+            for dst, src in zip(host[l], (K8[l], V8[l], KS[l], VS[l])):
+                dst.copy_(src, non_blocking=True)
+    e2e_steps = max(3, min(args.steps, 5))
+    ms_e2e = timed(e2e_step, e2e_steps)
+    d2h = L * (2 * hkv * n * D + 2 * hkv * nb * 4)
+
+    peak, src = measured_peak()
+    achieved = fp8_bytes / (launch_ms / 1e3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = export_cpu_baseline()
+    line = {"metric": "KV export to head-major e4m3 + block scales, algorithmic HBM GB/s, 36 layers x 32k tokens",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "config 3's KV cache exported (KV format row): 36 layers x 32768 tokens, "
+                                   "Hkv 8, D 128, fragmented 4096-page pools",
+                       "layers": L, "ctx": n, "n_kv_heads": hkv, "head_dim": D, "pool_pages": pages,
+                       "l2": "inputs larger than L2 (36 x 128 MiB of pages per step), no flush"},
+            "gpu_launches": L * args.steps,
+            "bf16_export_gbs": round(bf16_bytes * L / (ms_bf16 / 1e3) / 1e9, 1),
+            "fp8_import_gbs": round(fp8_bytes * L / (ms_import / 1e3) / 1e9, 1),
+            "e2e": {"value": round(fp8_bytes * L / (ms_e2e / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 3),
+                    "what": "export + device-to-host copy of the e4m3 output into pinned memory"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None, "peak_source": src,
+                         "kernel": "kv_export_kernel", "bytes_per_launch": fp8_bytes,
+                         "launch_ms": round(launch_ms, 5)},
+            "cpu_baseline": cpu,
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+def export_cpu_baseline():
+    """The oracle's export (a scalar C port; the reference has no export) on a
+    bounded sample: one layer of 4096 tokens, Hkv 8."""
+    import numpy as np
+    from oracle.oracle import Oracle
+    o = Oracle()
+    hkv, n, pages = HKV, 4096, 256
+    rng = np.random.default_rng(1)
+    kp = rng.integers(0, 0x4000, size=(pages, 16, hkv, D), dtype=np.uint16)
+    vp = rng.integers(0, 0x4000, size=(pages, 16, hkv, D), dtype=np.uint16)
+    ids = rng.permutation(pages).astype(np.int32)
+    reps, t = 0, 0.0
+    while t < 10.0 and reps < 50:
+        h0 = time.perf_counter()
+        o.export_kv(kp, vp, ids, ids, n, hkv, fp8=True)
+        t += time.perf_counter() - h0
+        reps += 1
+    nbytes = 2 * hkv * n * D * 3 + 2 * hkv * (n // 16) * 4
+    return {"value": round(nbytes * reps / t / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"oracle export of one layer, 4096 tokens x 8 heads, {reps} repetitions"}
+
+
 def run_qknorm(args):
     """Config 3 on the projections: each layer-token's Q/K/V arrive as the
     Q/K/V projections ([1, H*128] bf16) and go through QK-norm + RoPE before
@@ -497,6 +672,9 @@ def main():
         return
     if args.workload == "flash":
         run_flash(args)
+        return
+    if args.workload == "export":
+        run_export(args)
         return
 
     import torch

@@ -23,6 +23,7 @@ GKV_ERR_STATE = 5
 GKV_ERR_DEVICE = 6
 
 GKV_F32, GKV_F16, GKV_BF16 = 0, 1, 30
+GKV_KV_BF16, GKV_KV_FP8_E4M3 = 0, 1  # gkv_kv_format
 
 i32 = C.c_int32
 vp = C.c_void_p
@@ -94,6 +95,11 @@ SIGNATURES = {
     "gkv_rope_cache": ([C.c_float, i32, i32, vp, vp], C.c_int),
     "gkv_flash_attention": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, C.c_float, i32, i32, i32, vp], C.c_int),
     "gkv_flash_check_errors": ([u32p], C.c_int),
+    "gkv_export_kv_raw": ([C.POINTER(PoolDesc), vp, i32, i32, vp, vp, vp, vp, vp], C.c_int),
+    "gkv_import_kv_raw": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), i32, vp, vp, vp, vp, i32, vp],
+                          C.c_int),
+    "gkv_export_kv": ([vp, i32, i32, vp, vp, vp, vp, i32p, vp], C.c_int),
+    "gkv_import_kv": ([vp, i32, i32, vp, vp, vp, vp, i32, vp], C.c_int),
     "gkv_decode_layers": ([vp, i32, i32p, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), i32, C.c_float,
                            i32, vp], C.c_int),
     "gkv_qk_norm_rope": ([vp, vp, vp, i32, i32, i32, C.POINTER(QkNormDesc), i32, vp, vp, vp, vp], C.c_int),

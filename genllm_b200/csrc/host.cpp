@@ -260,11 +260,22 @@ gkv::NewPages pack(const gkv_new_pages* np, int32_t from, int32_t n) {
     return out;
 }
 
-// Publish new-page entries [from, to) of np with table-only launches.
+// Publish new-page entries [from, to) of np: table-only launches, or one
+// upload when there are many.
 int publish(const gkv_pool_desc* pool, gkv_table* t, const gkv_new_pages* np, int32_t from, int32_t to,
             cudaStream_t s) {
     gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
                      pool->pool_pages, pool->n_kv_heads};
+    if (to - from > gkv::kMaxNewPagesPerLaunch) {
+        // Many entries (an import of a long sequence, a long host-only
+        // growth): one stream-ordered upload instead of a launch per 64.
+        // Pageable source: the copy is staged before this call returns.
+        std::vector<int2> dev(to - from);
+        for (int32_t i = from; i < to; ++i) dev[i - from] = make_int2(np->k_ids[i], np->v_ids[i]);
+        cudaError_t e = cudaMemcpyAsync(t->d_table + np->first_new_page + from, dev.data(), sizeof(int2) * dev.size(),
+                                        cudaMemcpyHostToDevice, s);
+        return e == cudaSuccess ? GKV_OK : cuda_fail(e, "table upload");
+    }
     while (from < to) {
         const int32_t n = std::min<int32_t>(to - from, gkv::kMaxNewPagesPerLaunch);
         gkv::NewPages p = pack(np, from, n);
@@ -388,6 +399,64 @@ int gkv_append_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, 
     DeviceGuard g(t->device);
     if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", t->device);
     return append_chunks(pool, t, n_prior, np, K, V, seq_len, reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace {
+int check_format_buffers(int32_t format, const void* K, const void* V, const void* ks, const void* vs) {
+    if (format != GKV_KV_BF16 && format != GKV_KV_FP8_E4M3) return fail(GKV_ERR_INVALID, "unknown KV format %d", format);
+    if (!K || !V || !aligned16(K) || !aligned16(V))
+        return fail(GKV_ERR_INVALID, "K/V buffers must be non-null and 16-byte aligned");
+    if (format == GKV_KV_FP8_E4M3 &&
+        (!ks || !vs || reinterpret_cast<uintptr_t>(ks) % 4 || reinterpret_cast<uintptr_t>(vs) % 4))
+        return fail(GKV_ERR_INVALID, "the fp8 format needs 4-byte aligned scale buffers");
+    return GKV_OK;
+}
+}  // namespace
+
+int gkv_export_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_tokens, int32_t format, void* K_out,
+                      void* V_out, float* k_scales, float* v_scales, gkv_stream_t stream) {
+    int st = check_pool(pool);
+    if (st) return st;
+    if (!t || n_tokens < 0) return fail(GKV_ERR_INVALID, "gkv_export_kv_raw: bad arguments");
+    if (format != GKV_KV_BF16 && format != GKV_KV_FP8_E4M3) return fail(GKV_ERR_INVALID, "unknown KV format %d", format);
+    if (n_tokens == 0) return GKV_OK;
+    if ((st = check_format_buffers(format, K_out, V_out, k_scales, v_scales))) return st;
+    const int32_t n_pages = (n_tokens + 15) / 16;
+    if (n_pages > t->capacity)
+        return fail(GKV_ERR_INVALID, "%d tokens need %d table entries, table holds %d", n_tokens, n_pages, t->capacity);
+    DeviceGuard g(t->device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", t->device);
+    gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
+                     pool->pool_pages, pool->n_kv_heads};
+    cudaError_t e = gkv::launch_export(pv, t->d_table, n_tokens, format == GKV_KV_FP8_E4M3 ? 1 : 0, K_out, V_out,
+                                       k_scales, v_scales, t->scratch.err, t->num_sms,
+                                       reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? GKV_OK : cuda_fail(e, "export launch");
+}
+
+int gkv_import_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
+                      int32_t format, const void* K_in, const void* V_in, const float* k_scales,
+                      const float* v_scales, int32_t seq_len, gkv_stream_t stream) {
+    if (format == GKV_KV_BF16) return gkv_append_kv_raw(pool, t, n_prior, np, K_in, V_in, seq_len, stream);
+    int st = check_pool(pool);
+    if (st) return st;
+    if (format != GKV_KV_FP8_E4M3) return fail(GKV_ERR_INVALID, "unknown KV format %d", format);
+    if (!t || n_prior < 0 || seq_len < 0) return fail(GKV_ERR_INVALID, "gkv_import_kv_raw: bad arguments");
+    if (seq_len > 0 && (st = check_format_buffers(format, K_in, V_in, k_scales, v_scales))) return st;
+    const int32_t n_pages = (n_prior + seq_len + 15) / 16;
+    if ((st = check_new_pages(t, np, n_pages, pool->pool_pages))) return st;
+    DeviceGuard g(t->device);
+    if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", t->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // The table entries go out first (table-only launch), then the import
+    // kernel reads them from the device table.
+    if ((st = publish(pool, t, np, 0, np ? np->n_new_pages : 0, s))) return st;
+    if (seq_len == 0) return GKV_OK;
+    gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
+                     pool->pool_pages, pool->n_kv_heads};
+    cudaError_t e = gkv::launch_import_fp8(pv, t->d_table, n_prior, seq_len, K_in, V_in, k_scales, v_scales,
+                                           t->scratch.err, t->num_sms, s);
+    return e == cudaSuccess ? GKV_OK : cuda_fail(e, "import launch");
 }
 
 namespace {
@@ -957,6 +1026,50 @@ int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids
                                  L->n_kv_heads, scale, 1, n_q_heads / L->n_kv_heads, L->dtype, out_dtype, stream);
         if (st) return st;
     }
+    return GKV_OK;
+}
+
+int gkv_export_kv(gkv_manager* m, int32_t layer_id, int32_t format, void* K_out, void* V_out, float* k_scales,
+                  float* v_scales, int32_t* n_tokens, gkv_stream_t stream) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    gkv_pool_desc pool = pool_of(*L);
+    // Pages grown on the host only (gkv_append_kv_pages) reach the device table first.
+    gkv_new_pages np = pending(*L);
+    if (np.n_new_pages > 0) {
+        DeviceGuard g(L->table->device);
+        if (!g.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", L->table->device);
+        if ((st = check_new_pages(L->table, &np, static_cast<int32_t>(L->k_ids.size()), pool.pool_pages))) return st;
+        if ((st = publish(&pool, L->table, &np, 0, np.n_new_pages, reinterpret_cast<cudaStream_t>(stream)))) return st;
+        L->on_device = static_cast<int32_t>(L->k_ids.size());
+    }
+    if ((st = gkv_export_kv_raw(&pool, L->table, L->num_cached, format, K_out, V_out, k_scales, v_scales, stream)))
+        return st;
+    if (n_tokens) *n_tokens = L->num_cached;
+    return GKV_OK;
+}
+
+int gkv_import_kv(gkv_manager* m, int32_t layer_id, int32_t format, const void* K_in, const void* V_in,
+                  const float* k_scales, const float* v_scales, int32_t seq_len, gkv_stream_t stream) {
+    Layer* L = nullptr;
+    int st = ready_layer(m, layer_id, &L);
+    if (st) return st;
+    if (format != GKV_KV_BF16 && format != GKV_KV_FP8_E4M3) return fail(GKV_ERR_INVALID, "unknown KV format %d", format);
+    if (seq_len < 0) return fail(GKV_ERR_INVALID, "seq_len %d", seq_len);
+    if (seq_len == 0) return GKV_OK;
+    int32_t first = 0, n = 0;
+    if ((st = grow(*L, seq_len, &first, &n))) return st;
+    gkv_pool_desc pool = pool_of(*L);
+    gkv_new_pages np = pending(*L);
+    st = gkv_import_kv_raw(&pool, L->table, L->num_cached, &np, format, K_in, V_in, k_scales, v_scales, seq_len,
+                           stream);
+    if (st) {
+        ungrow(*L, first);
+        return st;
+    }
+    L->on_device = static_cast<int32_t>(L->k_ids.size());
+    L->num_cached += seq_len;
     return GKV_OK;
 }
 

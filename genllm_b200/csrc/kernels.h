@@ -85,6 +85,15 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
                           const DecodeLaunch& d, int num_sms, cudaStream_t stream,
                           const GatherLaunch* gather = nullptr);
 
+// export.cu: pages <-> dense head-major [Hkv][tokens][128] (bf16, or e4m3
+// with per (head, 16-token block) fp32 scales).
+cudaError_t launch_export(const PoolView& pool, const int2* table, int32_t n_tokens, int32_t fp8, void* k_out,
+                          void* v_out, float* k_scales, float* v_scales, uint32_t* err, int num_sms,
+                          cudaStream_t stream);
+cudaError_t launch_import_fp8(const PoolView& pool, const int2* table, int32_t n_prior, int32_t seq_len,
+                              const void* k_in, const void* v_in, const float* k_scales, const float* v_scales,
+                              uint32_t* err, int num_sms, cudaStream_t stream);
+
 // Scatter tokens [p_begin, p_end) of K/V ([Hkv][src_len][128]) to positions
 // n_prior + p, and publish np's entries to the table. With p_begin == p_end
 // only the table entries are written.

@@ -31,6 +31,7 @@ from ._lib import GKV_BF16, GKV_F16, GKV_F32, GkvError, check, lib
 PAGE_BLOCK_SIZE = 16
 
 _TORCH_TO_GKV = {torch.float32: GKV_F32, torch.float16: GKV_F16, torch.bfloat16: GKV_BF16}
+_GKV_TO_TORCH = {v: k for k, v in _TORCH_TO_GKV.items()}
 
 
 def _stream_handle(device: Optional[torch.device], stream=None):
@@ -164,6 +165,46 @@ class PagedAttentionManager:
         hkv, s, d = Kc.shape
         check(lib().gkv_append_kv(self.handle, layer_id, C.c_void_p(Kc.data_ptr()), C.c_void_p(Vc.data_ptr()),
                                   hkv, s, d, _TORCH_TO_GKV[Kc.dtype], _stream_handle(self.device, stream)))
+
+    # -- format export / import (no reference counterpart) --------------
+    def export_kv(self, layer_id: int, fp8: bool = False, stream=None):
+        """The layer's cached tokens as dense head-major tensors [Hkv, n, D]:
+        ``(K, V)`` in the pool dtype, or with ``fp8`` ``(K, V, k_scales,
+        v_scales)``, K/V ``float8_e4m3fn`` and scales fp32 [Hkv, ceil(n/16)]
+        (one per head and 16-token block). gkv_export_kv."""
+        info = self._info(layer_id)
+        n, hkv, d = info.num_cached, info.n_kv_heads, info.head_dim
+        dt = torch.float8_e4m3fn if fp8 else _GKV_TO_TORCH[info.dtype]
+        K = torch.empty((hkv, n, d), dtype=dt, device=self.device)
+        V = torch.empty_like(K)
+        nb = (n + PAGE_BLOCK_SIZE - 1) // PAGE_BLOCK_SIZE
+        ks = torch.empty((hkv, nb), dtype=torch.float32, device=self.device) if fp8 else None
+        vs = torch.empty_like(ks) if fp8 else None
+        got = C.c_int32()
+        check(lib().gkv_export_kv(self.handle, layer_id, _lib.GKV_KV_FP8_E4M3 if fp8 else _lib.GKV_KV_BF16,
+                                  C.c_void_p(K.data_ptr()), C.c_void_p(V.data_ptr()),
+                                  C.c_void_p(ks.data_ptr() if fp8 else 0), C.c_void_p(vs.data_ptr() if fp8 else 0),
+                                  C.byref(got), _stream_handle(self.device, stream)))
+        return (K, V, ks, vs) if fp8 else (K, V)
+
+    def import_kv(self, layer_id: int, K: torch.Tensor, V: torch.Tensor, k_scales: Optional[torch.Tensor] = None,
+                  v_scales: Optional[torch.Tensor] = None, stream=None) -> None:
+        """Append dense head-major tokens [Hkv, S, D] to the layer: in the pool
+        dtype (== append_kv_from_tensor), or e4m3 (``float8_e4m3fn`` / uint8)
+        with their fp32 block scales [Hkv, ceil(S/16)]. gkv_import_kv."""
+        Kc, Vc = _kv_view(K), _kv_view(V)
+        fp8 = Kc.dtype in (torch.float8_e4m3fn, torch.uint8)
+        if fp8 and (k_scales is None or v_scales is None):
+            raise GkvError(_lib.GKV_ERR_INVALID, "e4m3 K/V need their block scales")
+        if fp8:
+            for t in (k_scales, v_scales):
+                if t.dtype != torch.float32 or not t.is_contiguous() or t.device != Kc.device:
+                    raise GkvError(_lib.GKV_ERR_INVALID, "scales must be contiguous fp32 on K's device")
+        check(lib().gkv_import_kv(self.handle, layer_id, _lib.GKV_KV_FP8_E4M3 if fp8 else _lib.GKV_KV_BF16,
+                                  C.c_void_p(Kc.data_ptr()), C.c_void_p(Vc.data_ptr()),
+                                  C.c_void_p(k_scales.data_ptr() if fp8 else 0),
+                                  C.c_void_p(v_scales.data_ptr() if fp8 else 0), Kc.shape[1],
+                                  _stream_handle(self.device, stream)))
 
     # -- page_attention.cpp:205-216 -------------------------------------
     def reset(self) -> None:

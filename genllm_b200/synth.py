@@ -181,3 +181,30 @@ def heads_major(flat: np.ndarray, n_heads: int) -> np.ndarray:
     S = flat.shape[0]
     return np.ascontiguousarray(flat.reshape(S, n_heads, -1).transpose(1, 0, 2))
 
+
+
+def kv_format_values(seed: int, n_kv_heads: int, n_tokens: int, head_dim: int = 128,
+                     special: bool = True) -> tuple[np.ndarray, np.ndarray]:
+    """K and V [Hkv][n_tokens][D] bf16 bits for the format export / import
+    cases: N(0, 1) values with a different magnitude per 16-token block
+    (2^-20 .. 2^20), and with ``special`` the edge cases of the fp8 block
+    scale: an all-zero block, +-inf and NaN among finite values, a block of
+    bf16 subnormals and one of the largest finite bf16 values."""
+    rng = np.random.default_rng(seed)
+    n_blocks = (n_tokens + 15) // 16
+    out = []
+    for _ in range(2):
+        x = rng.standard_normal((n_kv_heads, n_tokens, head_dim), dtype=np.float32)
+        mag = np.exp2(rng.integers(-20, 21, size=(n_kv_heads, n_blocks))).astype(np.float32)
+        x *= np.repeat(mag, 16, axis=1)[:, :n_tokens, None]
+        b = bf16_bits(x)
+        if special and n_tokens >= 16:
+            h = n_kv_heads - 1
+            blk = lambda i: slice(16 * (i % n_blocks), min(n_tokens, 16 * (i % n_blocks) + 16))
+            b[0, blk(1)] = 0                                  # all-zero block
+            b[h, blk(2)][0, :3] = [0x7F80, 0xFF80, 0x7FC0]    # +inf, -inf, NaN
+            b[0, blk(3)] = (rng.integers(1, 0x80, b[0, blk(3)].shape) |
+                            (rng.integers(0, 2, b[0, blk(3)].shape) << 15)).astype(np.uint16)  # subnormals
+            b[h, blk(4)][:, ::7] = 0x7F7F                     # largest finite bf16
+        out.append(b)
+    return out[0], out[1]

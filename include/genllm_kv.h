@@ -370,6 +370,44 @@ int gkv_flash_attention(const void* Q, const void* K, const void* V, void* out, 
                         int32_t dtype, int32_t out_dtype, gkv_stream_t stream);
 int gkv_flash_check_errors(uint32_t* flags);
 
+/* ---------------- KV format export / import -------------------------------
+ * The reference keeps a layer's cache only in its page layout
+ * (src/core/page_attention.cpp:128) and cannot read it back. These entry
+ * points move a layer's first n_tokens tokens between the pages and a dense
+ * head-major copy [Hkv][n_tokens][128] (the layout append_kv_from_tensor
+ * takes, src/core/page_attention.cpp:104-139), in one of two formats:
+ *   GKV_KV_BF16: the pool's own bf16 bytes; export then append is the identity.
+ *   GKV_KV_FP8_E4M3: one byte per element plus one fp32 scale per (head,
+ *     16-token block), scales [Hkv][ceil(n_tokens / 16)]:
+ *       amax  = max |x| over the block's finite elements
+ *       scale = amax / 448, inv = 448 / amax (both 1 when 448 / amax is
+ *               not finite: amax 0, or below ~2^-119)
+ *       byte  = e4m3(x * inv): round to nearest even, finite overflow and
+ *               infinities saturate at +-448, NaN -> 0x7F
+ *     import: x' = bf16(e4m3_value(byte) * scale), bf16 rounded as the
+ *     reference rounds (include/utils/bfloat16.hpp:18-45).
+ * Device buffers, 16-byte aligned; stream-ordered, nothing synchronises. */
+typedef enum gkv_kv_format { GKV_KV_BF16 = 0, GKV_KV_FP8_E4M3 = 1 } gkv_kv_format;
+
+/* Raw tier: tokens [0, n_tokens) of the table's pages. k_scales / v_scales
+ * are used (and required) for GKV_KV_FP8_E4M3 only. */
+int gkv_export_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_tokens, int32_t format, void* K_out,
+                      void* V_out, float* k_scales, float* v_scales, gkv_stream_t stream);
+/* Raw tier: the inverse, seq_len tokens into positions [n_prior, n_prior +
+ * seq_len), table delta as gkv_append_kv_raw. Scales are indexed by 16-token
+ * blocks of the INPUT ([Hkv][ceil(seq_len / 16)]). GKV_KV_BF16 is
+ * gkv_append_kv_raw. */
+int gkv_import_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
+                      int32_t format, const void* K_in, const void* V_in, const float* k_scales,
+                      const float* v_scales, int32_t seq_len, gkv_stream_t stream);
+/* Managed tier: export the layer's cached tokens (*n_tokens receives the
+ * count; the buffers must hold it, see gkv_get_layer_info), or append
+ * seq_len imported tokens to the layer (pages allocated as gkv_append_kv). */
+int gkv_export_kv(gkv_manager* m, int32_t layer_id, int32_t format, void* K_out, void* V_out, float* k_scales,
+                  float* v_scales, int32_t* n_tokens, gkv_stream_t stream);
+int gkv_import_kv(gkv_manager* m, int32_t layer_id, int32_t format, const void* K_in, const void* V_in,
+                  const float* k_scales, const float* v_scales, int32_t seq_len, gkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

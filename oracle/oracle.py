@@ -84,6 +84,14 @@ class Oracle:
         L.orc_rope_cache.restype = None
         L.orc_flash_attention_f32.argtypes = [_vp, _vp, _vp] + [C.c_int32] * 6 + [C.c_float, C.c_int, _vp]
         L.orc_flash_attention_f32.restype = None
+        L.orc_e4m3_from_f32.argtypes = [C.c_float]
+        L.orc_e4m3_from_f32.restype = C.c_uint8
+        L.orc_e4m3_to_f32.argtypes = [C.c_uint8]
+        L.orc_e4m3_to_f32.restype = C.c_float
+        L.orc_export_kv.argtypes = [_vp, _vp, _vp, _vp] + [C.c_int32] * 3 + [C.c_int, _vp, _vp, _vp, _vp]
+        L.orc_export_kv.restype = None
+        L.orc_import_fp8.argtypes = [_vp, _vp, _vp, _vp, C.c_int32, _vp, _vp, _vp, _vp] + [C.c_int32] * 3
+        L.orc_import_fp8.restype = None
 
     def paged_attention_f32(self, q, k_pool, v_pool, k_ids, v_ids, total, n_q_heads, n_kv_heads,
                             seq_len, head_dim, scale, causal=True, dtype=BF16, threads=0):
@@ -145,6 +153,40 @@ class Oracle:
         sin = np.empty((max_seq, head_dim), dtype=np.float32)
         self.lib.orc_rope_cache(theta, head_dim, max_seq, _ptr(cos), _ptr(sin))
         return cos, sin
+
+    def e4m3_from_f32(self, x: np.ndarray) -> np.ndarray:
+        """Elementwise OCP e4m3 encoding (kv_format_oracle.c), uint8."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        return np.array([self.lib.orc_e4m3_from_f32(float(v)) for v in x], dtype=np.uint8)
+
+    def e4m3_to_f32(self, b: np.ndarray) -> np.ndarray:
+        b = np.ascontiguousarray(b, dtype=np.uint8).ravel()
+        return np.array([self.lib.orc_e4m3_to_f32(int(v)) for v in b], dtype=np.float32)
+
+    def export_kv(self, k_pool, v_pool, k_ids, v_ids, n_tokens, n_kv_heads, head_dim=128, fp8=False):
+        """Pages -> dense [Hkv][n_tokens][D]: uint16 (bf16) or uint8 (e4m3) arrays,
+        plus fp32 scales [Hkv][blocks] for fp8 (None for bf16)."""
+        k_ids = np.ascontiguousarray(k_ids, dtype=np.int32)
+        v_ids = np.ascontiguousarray(v_ids, dtype=np.int32)
+        dt = np.uint8 if fp8 else np.uint16
+        ko = np.zeros((n_kv_heads, n_tokens, head_dim), dtype=dt)
+        vo = np.zeros_like(ko)
+        nb = (n_tokens + 15) // 16
+        ks = np.zeros((n_kv_heads, nb), dtype=np.float32)
+        vs = np.zeros_like(ks)
+        self.lib.orc_export_kv(_ptr(k_pool), _ptr(v_pool), _ptr(k_ids), _ptr(v_ids), n_tokens, n_kv_heads, head_dim,
+                               int(bool(fp8)), _ptr(ko), _ptr(vo), _ptr(ks), _ptr(vs))
+        return ko, vo, (ks if fp8 else None), (vs if fp8 else None)
+
+    def import_fp8(self, k_pool, v_pool, k_ids, v_ids, n_prior, k_in, v_in, k_scales, v_scales):
+        """Dequantise e4m3 [Hkv][S][D] into the pools in place (kv_format_oracle.c)."""
+        k_ids = np.ascontiguousarray(k_ids, dtype=np.int32)
+        v_ids = np.ascontiguousarray(v_ids, dtype=np.int32)
+        k_in, v_in = (np.ascontiguousarray(a, dtype=np.uint8) for a in (k_in, v_in))
+        k_scales, v_scales = (np.ascontiguousarray(a, dtype=np.float32) for a in (k_scales, v_scales))
+        Hkv, S, D = k_in.shape
+        self.lib.orc_import_fp8(_ptr(k_pool), _ptr(v_pool), _ptr(k_ids), _ptr(v_ids), n_prior, _ptr(k_in),
+                                _ptr(v_in), _ptr(k_scales), _ptr(v_scales), S, Hkv, D)
 
     def flash_attention_f32(self, q, k, v, scale, causal=True):
         """q uint16 [B][Hq][S][D], k/v [B][Hkv][S][D] -> fp32 [B][Hq][S][D]

@@ -116,6 +116,18 @@ void orc_flash_attention_f32(const uint16_t* q, const uint16_t* k, const uint16_
                              int32_t Hkv, int32_t S, int32_t D, int32_t groups, float scale, int causal,
                              float* out);
 
+/* kv_format_oracle.c: KV export / import between pages and dense head-major
+ * [Hkv][tokens][D] (bf16, or OCP e4m3 with per (head, 16-token block) fp32
+ * scales [Hkv][blocks]). */
+uint8_t orc_e4m3_from_f32(float f);
+float orc_e4m3_to_f32(uint8_t b);
+void orc_export_kv(const uint16_t* k_pool_base, const uint16_t* v_pool_base, const int32_t* k_ids,
+                   const int32_t* v_ids, int32_t n_tokens, int32_t n_kv_heads, int32_t head_dim, int fp8,
+                   void* k_out, void* v_out, float* k_scales, float* v_scales);
+void orc_import_fp8(uint16_t* k_pool_base, uint16_t* v_pool_base, const int32_t* k_ids, const int32_t* v_ids,
+                    int32_t n_prior, const uint8_t* k_in, const uint8_t* v_in, const float* k_scales,
+                    const float* v_scales, int32_t seq_len, int32_t n_kv_heads, int32_t head_dim);
+
 /* Round an fp32 buffer to the reference's bf16 (RNE, subnormals to signed 0). */
 void orc_round_bf16(const float* in, uint16_t* out, size_t n);
 

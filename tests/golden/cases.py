@@ -35,3 +35,15 @@ FLASH = [
     ("flash_b1_noncausal", 42, 1, 4, 4, 20, False),
 ]
 
+
+# KV format export / import: (name, seed, Hkv, [token counts of the
+# reference's successive append calls], pool pages). The fixtures hold the
+# pages and block table the reference's own append_kv_from_tensor produced,
+# checksums of the appended K/V (= the expected bf16 export, regenerated from
+# the seed by genllm_b200.synth.kv_format_values), and the expected fp8 export
+# (bytes and block scales) computed with numpy fp32 arithmetic and torch's
+# float8_e4m3fn conversion.
+KV_FORMAT = [
+    ("kvfmt_ragged", 51, 2, [21, 16], 8),
+    ("kvfmt_heads8", 52, 8, [100, 1, 1, 50], 10),
+]

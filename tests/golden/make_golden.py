@@ -18,9 +18,9 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, HERE)
 
-from cases import CONFIG1, FLASH, QK_ROPE, SMALL  # noqa: E402
+from cases import CONFIG1, FLASH, KV_FORMAT, QK_ROPE, SMALL  # noqa: E402
 from genllm_b200.synth import fragmented_case, heads_major, qk_rope_case  # noqa: E402
-from oracle.oracle import RefOps, ref_flash_attention, run_ref_case  # noqa: E402
+from oracle.oracle import RefOps, RefSession, ref_flash_attention, run_ref_case  # noqa: E402
 
 
 def sha(a: np.ndarray) -> str:
@@ -47,6 +47,7 @@ def main():
     print(name, out.shape, nc)
     make_qk_rope()
     make_flash()
+    make_kv_format()
 
 
 def flash_inputs(seed, B, Hq, Hkv, S):
@@ -82,6 +83,55 @@ def make_qk_rope():
                             cache_sha=np.array([sha(cos), sha(sin)]),
                             inputs_sha=np.array([sha(c.q_flat), sha(c.k_flat), sha(c.q_norm_w), sha(c.k_norm_w)]))
         print(name, qr.shape, kr.shape)
+
+
+def fp8_export_numpy(x_bits: np.ndarray):
+    """Expected e4m3 export of [H][n][D] bf16 bits, independent of the C
+    oracle: numpy fp32 block amax / scale / product, torch's float8_e4m3fn
+    conversion (round to nearest even) after clamping to +-448, NaN -> 0x7F."""
+    import torch
+    H, n, D = x_bits.shape
+    nb = (n + 15) // 16
+    x = (x_bits.astype(np.uint32) << 16).view(np.float32)
+    q = np.zeros(x.shape, np.uint8)
+    scales = np.zeros((H, nb), np.float32)
+    for h in range(H):
+        for b in range(nb):
+            blk = x[h, 16 * b:16 * b + 16]
+            a = np.abs(blk[np.isfinite(blk)])
+            amax = np.float32(a.max()) if a.size else np.float32(0)
+            with np.errstate(divide="ignore", over="ignore"):
+                inv = np.float32(448) / amax
+            scale = amax / np.float32(448) if np.isfinite(inv) else np.float32(1)
+            inv = inv if np.isfinite(inv) else np.float32(1)
+            y = np.clip(blk * inv, np.float32(-448), np.float32(448)).astype(np.float32)
+            e = torch.from_numpy(np.ascontiguousarray(y)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+            q[h, 16 * b:16 * b + 16] = np.where(np.isnan(y), np.uint8(0x7F), e)
+            scales[h, b] = scale
+    return q, scales
+
+
+def make_kv_format():
+    """Pages from the reference's append_kv_from_tensor
+    (src/core/page_attention.cpp:104-139), called once per chunk."""
+    from genllm_b200.synth import kv_format_values
+    for name, seed, hkv, chunks, pages in KV_FORMAT:
+        n = sum(chunks)
+        K, V = kv_format_values(seed, hkv, n)
+        R = RefSession(1, hkv, 128, pages)
+        p0 = 0
+        for c in chunks:
+            R.append_kv(0, np.ascontiguousarray(K[:, p0:p0 + c]), np.ascontiguousarray(V[:, p0:p0 + c]), c)
+            p0 += c
+        k_ids, v_ids, nc = R.table(0)
+        kq, ks = fp8_export_numpy(K)
+        vq, vs = fp8_export_numpy(V)
+        # K and V themselves are regenerated from the seed (checksums here).
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), k_pool=R.pool_view(0, 0).copy(),
+                            v_pool=R.pool_view(0, 1).copy(), k_ids=k_ids, v_ids=v_ids, num_cached=nc,
+                            kv_sha=np.array([sha(K), sha(V)]), k_fp8=kq, v_fp8=vq, k_scales=ks, v_scales=vs)
+        R.close()
+        print(name, K.shape, nc, len(k_ids))
 
 
 if __name__ == "__main__":

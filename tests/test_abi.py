@@ -51,3 +51,23 @@ def test_new_entry_points_reject_bad_arguments_without_a_gpu():
     s = np.zeros((4, 128), np.float32)
     assert L.gkv_rope_cache(1e6, 128, 4, C.c_void_p(c.ctypes.data), C.c_void_p(s.ctypes.data)) == 0
     assert c[0, 0] == 1.0 and s[0, 0] == 0.0
+
+
+def test_kv_format_entry_points_reject_bad_arguments_without_a_gpu():
+    import ctypes as C
+    L = _lib.lib()
+    assert L.gkv_export_kv_raw(None, None, 16, 0, None, None, None, None, None) == _lib.GKV_ERR_INVALID
+    assert L.gkv_import_kv_raw(None, None, 0, None, 1, None, None, None, None, 16, None) == _lib.GKV_ERR_INVALID
+    pool = _lib.PoolDesc(C.c_void_p(16), C.c_void_p(16), 4, 2, 128, _lib.GKV_BF16)
+    # unknown format; a missing table
+    assert L.gkv_export_kv_raw(C.byref(pool), None, 16, 7, None, None, None, None, None) == _lib.GKV_ERR_INVALID
+    assert L.gkv_import_kv_raw(C.byref(pool), None, 0, None, 7, None, None, None, None, 16, None) == \
+        _lib.GKV_ERR_INVALID
+    # a host-only manager has no device pools
+    m = C.c_void_p()
+    assert L.gkv_manager_create(-1, C.byref(m)) == 0
+    assert L.gkv_init_layer(m, 0, 2, 128, _lib.GKV_BF16) == 0
+    n = C.c_int32(-1)
+    assert L.gkv_export_kv(m, 0, 0, None, None, None, None, C.byref(n), None) == _lib.GKV_ERR_STATE
+    assert L.gkv_import_kv(m, 0, 1, None, None, None, None, 4, None) == _lib.GKV_ERR_STATE
+    assert L.gkv_manager_destroy(m) == 0
