@@ -124,13 +124,13 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def profiled_traffic(args, world):
-    """DRAM bytes (read + write) of one paged_decode_kernel launch from the
+def profiled_traffic(args, world, summary="paged_decode_kernel_qwen3_4b_32k.md"):
+    """DRAM bytes (read + write) of one launch of the summary's kernel from the
     committed ncu summary of this exact configuration, or None."""
     if world != 1 or args.ctx != CTX:
         return None
     try:
-        with open(os.path.join(ROOT, "profiles", "paged_decode_kernel_qwen3_4b_32k.md")) as f:
+        with open(os.path.join(ROOT, "profiles", summary)) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch:"):
                     return int(line.split(":")[1])
@@ -504,8 +504,9 @@ def run_export(args):
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 3),
                     "what": "export + device-to-host copy of the e4m3 output into pinned memory"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None, "peak_source": src,
-                         "kernel": "kv_export_kernel", "bytes_per_launch": fp8_bytes,
+                         "frac": round(achieved / peak, 4),
+                         "traffic": profiled_traffic(args, 1, "kv_export_kernel_qwen3_4b_32k.md"),
+                         "peak_source": src, "kernel": "kv_export_kernel", "bytes_per_launch": fp8_bytes,
                          "launch_ms": round(launch_ms, 5)},
             "cpu_baseline": cpu,
             "clocks": clk}
