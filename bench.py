@@ -787,17 +787,23 @@ def main():
     h_in.copy_(wl.inbuf)
     h_out = torch.empty((args.layers, (HQ if world > 1 else hq_l) * D), dtype=torch.bfloat16).pin_memory()
 
-    from genllm_b200.paged_attention import DecodeStep
-    one_call = None
+    from genllm_b200.paged_attention import DecodeGraph, DecodeStep
+    one_call = graph = None
     if hg is None and world == 1:
-        # The whole step's 36 layers through one library call.
-        one_call = DecodeStep(wl.mgr, list(range(args.layers)), [b.q for b in wl.layers], [b.k for b in wl.layers],
-                              [b.v for b in wl.layers], [b.out for b in wl.layers], hq_l, wl.scale)
+        # The whole step's 36 layers through one library call, and the same
+        # step captured as a CUDA graph (one graph launch per step).
+        bound = ([b.q for b in wl.layers], [b.k for b in wl.layers], [b.v for b in wl.layers],
+                 [b.out for b in wl.layers])
+        one_call = DecodeStep(wl.mgr, list(range(args.layers)), *bound, hq_l, wl.scale)
+        graph = DecodeGraph(wl.mgr, list(range(args.layers)), *bound, hq_l, wl.scale)
+    enqueue = [0.0]
 
-    def e2e_step():
+    def e2e_step(runner=None):
         wl.inbuf.copy_(h_in, non_blocking=True)
-        if one_call is not None:
-            one_call.run()
+        if runner is not None:
+            h0 = time.perf_counter()
+            runner.run()
+            enqueue[0] += time.perf_counter() - h0
             h_out.copy_(wl.outbuf, non_blocking=True)
             torch.cuda.current_stream().synchronize()
             return float(h_out[-1, 0])
@@ -813,28 +819,45 @@ def main():
         torch.cuda.current_stream().synchronize()
         return float(h_out[-1, 0])  # the step's result, read on the host
 
-    for _ in range(2):
-        e2e_step()
-    ctx1 = wl.cached(0)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e_ms = e0.elapsed_time(e1)
-    eb = 0
-    for k in range(e2e_steps):
-        eb += args.layers * wl.bytes_per_layer_token(ctx1 + k + 1)
-    te = torch.tensor([e_ms], device="cuda")
-    be = torch.tensor([float(eb)], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        dist.all_reduce(be, op=dist.ReduceOp.SUM)
-    e2e_value = be.item() / (te.item() / 1e3) / 1e9
+    def e2e_run(runner):
+        for _ in range(2):
+            e2e_step(runner)
+        ctx1 = wl.cached(0)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        enqueue[0] = 0.0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step(runner)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        eb = 0
+        for k in range(e2e_steps):
+            eb += args.layers * wl.bytes_per_layer_token(ctx1 + k + 1)
+        te = torch.tensor([e_ms], device="cuda")
+        be = torch.tensor([float(eb)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            dist.all_reduce(be, op=dist.ReduceOp.SUM)
+        return be.item() / (te.item() / 1e3) / 1e9, te.item() / e2e_steps, 1e3 * enqueue[0] / e2e_steps
+
+    extra_e2e = {}
+    if graph is not None:
+        v1, ms1, enq1 = e2e_run(one_call)
+        extra_e2e = {"one_call": {"value": round(v1, 2), "ms_per_step": round(ms1, 4),
+                                  "host_call_ms_per_step": round(enq1, 4),
+                                  "path": "same copies, one gkv_decode_layers call per step"}}
+        e2e_value, e2e_ms, e2e_enq = e2e_run(graph)
+        e2e_path = ("one pinned H2D copy of all layers Q/K/V, one gkv_decode_graph_step call (C ABI: host page "
+                    "allocation + one CUDA-graph launch of the 36 layers' kernels), one D2H copy of the outputs, "
+                    "host reads the result")
+    else:
+        e2e_value, e2e_ms, e2e_enq = e2e_run(None)
+        e2e_path = ("one pinned H2D copy of all layers Q/K/V, per-layer C ABI calls, one D2H copy of the "
+                    "outputs, host reads the result")
     h2d = h_in.numel() * 2
     d2h = h_out.numel() * 2
 
@@ -855,11 +878,8 @@ def main():
         "us_per_token_layer": round(1e3 * ms_max / (args.steps * args.layers), 3),
         "tok_per_s_qwen3_4b_attention": round(args.steps / (ms_max / 1e3), 2),
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps, "ms_per_step": round(te.item() / e2e_steps, 4),
-                "path": ("one pinned H2D copy of all layers Q/K/V, one gkv_decode_layers call (C ABI) for the 36 "
-                         "layers, one D2H copy of the outputs, host reads the result" if one_call is not None else
-                         "one pinned H2D copy of all layers Q/K/V, per-layer C ABI calls, one D2H copy of the "
-                         "outputs, host reads the result")},
+                "steps": e2e_steps, "ms_per_step": round(e2e_ms, 4), "host_call_ms_per_step": round(e2e_enq, 4),
+                "path": e2e_path, **extra_e2e},
         "gpu_launches": 2 * args.steps * args.layers,
         "gather": (args.gather if world > 1 else None),
         "host_enqueue_ms_per_step": round(1e3 * host_enqueue_s / args.steps, 4),

@@ -95,6 +95,10 @@ SIGNATURES = {
     "gkv_rope_cache": ([C.c_float, i32, i32, vp, vp], C.c_int),
     "gkv_flash_attention": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, C.c_float, i32, i32, i32, vp], C.c_int),
     "gkv_flash_check_errors": ([u32p], C.c_int),
+    "gkv_decode_graph_create": ([vp, i32, i32p, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), i32,
+                                 C.c_float, i32, C.POINTER(C.POINTER(QkNormDesc)), C.POINTER(vp)], C.c_int),
+    "gkv_decode_graph_step": ([vp, vp], C.c_int),
+    "gkv_decode_graph_destroy": ([vp], C.c_int),
     "gkv_export_kv_raw": ([C.POINTER(PoolDesc), vp, i32, i32, vp, vp, vp, vp, vp], C.c_int),
     "gkv_import_kv_raw": ([C.POINTER(PoolDesc), vp, i32, C.POINTER(NewPages), i32, vp, vp, vp, vp, i32, vp],
                           C.c_int),

@@ -31,6 +31,8 @@
 // every mbarrier wait is bounded (kErrTimeout).
 #include <cstdlib>
 
+#include <atomic>
+
 #include "device.cuh"
 #include "kernels.h"
 #include "qk_rope.cuh"
@@ -78,6 +80,7 @@ struct DecodeParams {
     int32_t new_n;
     int32_t qk_on;  // 1: q / k_new are pre-norm projections: QK-norm + RoPE here (position n_prior)
     QkNorm qk;
+    const DeviceStep* step;  // non-null: the step fields above come from here (captured steps)
     float qscale;  // softmax scale * log2(e)
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
@@ -85,9 +88,27 @@ struct DecodeParams {
     int2 new_ids[kMaxNewPagesPerLaunch];
 };
 
-__device__ __forceinline__ int2 page_entry(const DecodeParams& a, int lp) {
-    const int r = lp - a.new_first;
-    if (r >= 0 && r < a.new_n) return a.new_ids[r];
+// The step fields, from the launch parameters or (captured steps) from the
+// device step block, which a copy before the step wrote: safe to read before
+// griddepcontrol.wait.
+struct StepFields {
+    int n_prior, total, n_pages, pages_per_split, new_first, new_n;
+    int2 new0;
+};
+
+__device__ __forceinline__ StepFields step_fields(const DecodeParams& a) {
+    if (a.step) {
+        const DeviceStep* s = a.step;
+        return {__ldg(&s->n_prior), __ldg(&s->total), __ldg(&s->n_pages), __ldg(&s->pages_per_split),
+                __ldg(&s->new_first), __ldg(&s->new_n), __ldg(&s->new_id)};
+    }
+    return {a.n_prior, a.total, a.n_pages, a.pages_per_split, a.new_first, a.new_n, a.new_ids[0]};
+}
+
+__device__ __forceinline__ int2 page_entry(const DecodeParams& a, const StepFields& sf, int lp) {
+    const int r = lp - sf.new_first;
+    if (r == 0 && sf.new_n > 0) return sf.new0;
+    if (r > 0 && r < sf.new_n) return a.new_ids[r];  // more than one new page: never a captured step
     return a.table[lp];
 }
 
@@ -145,13 +166,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int Hkv = a.n_kv_heads;
     const int G = a.group;
     const int P = a.pages_per_stage;
-    const int p0 = split * a.pages_per_split;
-    const int p1 = min(a.n_pages, p0 + a.pages_per_split);
+    const StepFields sf = step_fields(a);
+    const int p0 = split * sf.pages_per_split;
+    const int p1 = min(sf.n_pages, p0 + sf.pages_per_split);
     const int n_stages = p1 > p0 ? (p1 - p0 + P - 1) / P : 0;
 
     // Publish this step's new block-table entries (this launch reads them
     // from its parameters; later launches read the table).
-    if (split == 0 && (int)threadIdx.x < a.new_n) a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
+    if (split == 0 && (int)threadIdx.x < sf.new_n)
+        a.table[sf.new_first + threadIdx.x] = threadIdx.x == 0 ? sf.new0 : a.new_ids[threadIdx.x];
 
     // Programmatic dependent launch: the split-combine kernel that follows may
     // be scheduled now (it waits for this grid's completion itself).
@@ -182,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // A page id, bounds-checked: a bad id becomes {-1, -1} (loaded as page 0,
     // skipped by the consumer) and sets the error bit.
     auto checked = [&](int i) {
-        int2 e = page_entry(a, p0 + i);
+        int2 e = page_entry(a, sf, p0 + i);
         if (!entry_ok(a, e)) {
             atomicOr(a.err, kErrBadPage);
             e = make_int2(-1, -1);
@@ -233,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // covers theirs.
         RowParamsG8 rq;
         if (a.qk_on) {
-            const size_t pos = (size_t)a.n_prior * kHeadDim;
+            const size_t pos = (size_t)sf.n_prior * kHeadDim;
             rq = load_row_params_g8(a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, lane & 7);
         }
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -252,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 // the warp's 512-byte P buffer (idle until the first page),
                 // two at a time, from which each lane takes its fragment.
                 const int grp = lane >> 3, j = lane & 7;
-                const size_t pos = (size_t)a.n_prior * kHeadDim;
+                const size_t pos = (size_t)sf.n_prior * kHeadDim;
                 uint16_t* stage = reinterpret_cast<uint16_t*>(pbuf);
 #pragma unroll
                 for (int b0 = 0; b0 < 8; b0 += 4) {
@@ -331,15 +354,15 @@ __global__ void __launch_bounds__(kThreads, 2)
                 uint8_t* kt = smem + st * kStageBytes + (uint32_t)(pslot * Hkv + head) * kTile;
                 uint8_t* vt = kt + kStageKV;
                 const int base = lp * kPageSlots;
-                const int nvalid = min(kPageSlots, a.total - base);
+                const int nvalid = min(kPageSlots, sf.total - base);
                 // Fused append of this step's token.
-                if (a.k_new != nullptr && a.n_prior >= base && a.n_prior < base + kPageSlots) {
-                    const int slot = a.n_prior - base;
+                if (a.k_new != nullptr && sf.n_prior >= base && sf.n_prior < base + kPageSlots) {
+                    const int slot = sf.n_prior - base;
                     uint2 kk;
                     if (a.qk_on) {  // the post-QK-norm, post-RoPE row is what the page holds
                         float xk[4];
                         load_row4(a.k_new + (size_t)head * kHeadDim, lane, xk);
-                        const size_t pos = (size_t)a.n_prior * kHeadDim;
+                        const size_t pos = (size_t)sf.n_prior * kHeadDim;
                         const RowParams rp = load_row_params(a.qk.k_w, a.qk.cos + pos, a.qk.sin + pos, lane);
                         uint16_t o[4];
                         norm_rope_row(xk, rp, a.qk.eps, o);
@@ -538,6 +561,7 @@ struct CombineParams {
     int32_t n_splits;
     uint32_t* err;
     GatherLaunch g;
+    const DeviceStep* step;  // non-null: n_splits from here (captured steps)
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
 #endif
@@ -572,13 +596,14 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     __shared__ float s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims], s_m[kCombineWarps];
     // One pass with an online rescale: each batch's loads are issued together.
     float M = -INFINITY, L = 0.f, A = 0.f;
-    for (int b = 0; b * kBatch * kCombineWarps < c.n_splits; ++b) {
+    const int n_splits = c.step ? __ldg(&c.step->n_splits) : c.n_splits;
+    for (int b = 0; b * kBatch * kCombineWarps < n_splits; ++b) {
         float2 ml[kBatch];
         float av[kBatch];
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
             const int s = w + (b * kBatch + i) * kCombineWarps;
-            const bool in = s < c.n_splits;
+            const bool in = s < n_splits;
             ml[i] = in ? c.part_ml[(size_t)s * c.n_q_heads + hq] : make_float2(-INFINITY, 0.f);
             av[i] = in ? c.part_acc[((size_t)s * c.n_q_heads + hq) * kHeadDim + d] : 0.f;
         }
@@ -679,16 +704,12 @@ bool overlap_enabled() {
 
 }  // namespace
 
-cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map, int2* table,
-                          const NewPages& np, const Scratch& scratch, const DecodeLaunch& d, int num_sms,
-                          cudaStream_t stream, const GatherLaunch* gather) {
-    const int Hkv = pool.n_kv_heads;
-    if (Hkv > kConsumerWarps) return cudaErrorInvalidValue;
-    static unsigned long long configured = 0;
+cudaError_t configure_decode_kernels() {
+    static std::atomic<unsigned long long> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev >= 64 || !(configured & (1ull << dev))) {
+    if (dev >= 64 || !(configured.load() & (1ull << dev))) {
         e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
         if (e != cudaSuccess) return e;
         // Both kernels ask for the largest shared-memory carveout, so that an
@@ -698,8 +719,37 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(paged_decode_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
-        if (dev < 64) configured |= 1ull << dev;
+        if (dev < 64) configured.fetch_or(1ull << dev);
     }
+    return cudaSuccess;
+}
+
+bool decode_split_geometry(int32_t n_pages, int32_t n_kv_heads, int32_t n_q_heads, int32_t n_splits_hint,
+                           int num_sms, int32_t* pages_per_split, int32_t* n_splits_out) {
+    const int P = kConsumerWarps / n_kv_heads;
+    const int n_stages_total = (n_pages + P - 1) / P;
+    int n_splits = n_splits_hint > 0 ? n_splits_hint : num_sms;
+    if (n_splits > n_stages_total) n_splits = n_stages_total;
+    if (n_splits * n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / n_q_heads;
+    if (n_splits < 1) n_splits = 1;
+    int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
+    if (stages_per_split * P > kMaxSplitPages) {  // very long contexts: more splits than SMs
+        stages_per_split = kMaxSplitPages / P;
+        n_splits = (n_stages_total + stages_per_split - 1) / stages_per_split;
+        if (n_splits * n_q_heads > kMaxPartialRows) return false;
+    }
+    *pages_per_split = stages_per_split * P;
+    *n_splits_out = (n_pages + *pages_per_split - 1) / *pages_per_split;
+    return true;
+}
+
+cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map, int2* table,
+                          const NewPages& np, const Scratch& scratch, const DecodeLaunch& d, int num_sms,
+                          cudaStream_t stream, const GatherLaunch* gather) {
+    const int Hkv = pool.n_kv_heads;
+    if (Hkv > kConsumerWarps) return cudaErrorInvalidValue;
+    cudaError_t e = configure_decode_kernels();
+    if (e != cudaSuccess) return e;
     DecodeParams p;
     p.q = d.q;
     p.k_new = d.k_new;
@@ -729,20 +779,18 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     for (int i = 0; i < np.n; ++i) p.new_ids[i] = np.ids[i];
 
     // One CTA per SM; each split a whole number of stages.
-    const int P = p.pages_per_stage;
-    const int n_stages_total = (d.n_pages + P - 1) / P;
-    int n_splits = d.n_splits > 0 ? d.n_splits : num_sms;
-    if (n_splits > n_stages_total) n_splits = n_stages_total;
-    if (n_splits * d.n_q_heads > kMaxPartialRows) n_splits = kMaxPartialRows / d.n_q_heads;
-    if (n_splits < 1) n_splits = 1;
-    int stages_per_split = (n_stages_total + n_splits - 1) / n_splits;
-    if (stages_per_split * P > kMaxSplitPages) {  // very long contexts: more splits than SMs
-        stages_per_split = kMaxSplitPages / P;
-        n_splits = (n_stages_total + stages_per_split - 1) / stages_per_split;
-        if (n_splits * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
+    int n_splits = 0;
+    if (!decode_split_geometry(d.n_pages, Hkv, d.n_q_heads, d.n_splits, num_sms, &p.pages_per_split, &n_splits))
+        return cudaErrorInvalidValue;
+    p.step = d.step;
+    int grid = n_splits;
+    if (d.step) {
+        // Captured step: the geometry in the step block changes from token
+        // to token; the grid is fixed and splits past the step's count find
+        // no pages.
+        if (d.grid < 1 || d.grid * d.n_q_heads > kMaxPartialRows) return cudaErrorInvalidValue;
+        grid = d.grid;
     }
-    p.pages_per_split = stages_per_split * P;
-    n_splits = (d.n_pages + p.pages_per_split - 1) / p.pages_per_split;
 
     // Both launches use programmatic dependent launch: the decode grid's page
     // stream may start while the previous kernel on the stream finishes (it
@@ -752,7 +800,7 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = overlap_enabled() ? 1 : 0;
     cudaLaunchConfig_t dcfg = {};
-    dcfg.gridDim = dim3(n_splits);
+    dcfg.gridDim = dim3(grid);
     dcfg.blockDim = dim3(kThreads);
     dcfg.dynamicSmemBytes = kSmemBytes;
     dcfg.stream = stream;
@@ -763,6 +811,7 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
 
     CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits, scratch.err, {}};
     if (gather) c.g = *gather;
+    c.step = d.step;
 #ifdef GKV_PROBE_TIMELINE
     c.probe_slot = p.probe_slot;
 #endif

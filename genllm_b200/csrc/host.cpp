@@ -1029,6 +1029,246 @@ int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids
     return GKV_OK;
 }
 
+// ============================ captured decode steps ===========================
+
+struct gkv_decode_graph {
+    gkv_manager* m = nullptr;
+    int device = 0;
+    int grid = 0;
+    int32_t n_q_heads = 0;
+    std::vector<int32_t> layers;
+    std::vector<int32_t> max_seq;     // per layer: RoPE rows (0 without QK-norm)
+    gkv::DeviceStep* host[2] = {nullptr, nullptr};  // pinned, one per graph
+    gkv::DeviceStep* dev[2] = {nullptr, nullptr};
+    cudaGraphExec_t exec[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    bool launched[2] = {false, false};
+    uint64_t steps = 0;
+};
+
+namespace {
+
+void decode_graph_free(gkv_decode_graph* g) {
+    if (!g) return;
+    DeviceGuard dg(g->device);
+    for (int b = 0; b < 2; ++b) {
+        if (g->done[b]) {
+            cudaEventSynchronize(g->done[b]);
+            cudaEventDestroy(g->done[b]);
+        }
+        if (g->exec[b]) cudaGraphExecDestroy(g->exec[b]);
+        cudaFreeHost(g->host[b]);
+        cudaFree(g->dev[b]);
+    }
+    delete g;
+}
+
+// Capture buffer b's step: the copy of the step block, then every layer's
+// decode + combine launches reading it.
+int capture_decode_graph(gkv_decode_graph* g, int b, const void* const* Q, const void* const* K,
+                         const void* const* V, void* const* out, int32_t n_q_heads, float scale, int32_t out_dtype,
+                         const gkv::QkNorm* qks) {
+    cudaStream_t cs = nullptr;
+    cudaError_t e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_fail(e, "capture stream");
+    const size_t n = g->layers.size();
+    e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+    int st = GKV_OK;
+    if (e == cudaSuccess) {
+        e = cudaMemcpyAsync(g->dev[b], g->host[b], sizeof(gkv::DeviceStep) * n, cudaMemcpyHostToDevice, cs);
+        for (size_t i = 0; i < n && e == cudaSuccess; ++i) {
+            Layer* L = find_layer(g->m, g->layers[i]);
+            gkv_table* t = L->table;
+            gkv::PoolView pv{static_cast<uint16_t*>(L->k_base), static_cast<uint16_t*>(L->v_base), L->max_blocks,
+                             L->n_kv_heads};
+            gkv::DecodeLaunch d{};
+            d.q = static_cast<const uint16_t*>(Q[i]);
+            d.k_new = static_cast<const uint16_t*>(K[i]);
+            d.v_new = static_cast<const uint16_t*>(V[i]);
+            d.out = out[i];
+            d.out_dtype = out_dtype;
+            d.n_q_heads = n_q_heads;
+            d.n_prior = 0;  // capture-time values; the kernels read the step block
+            d.total = 1;
+            d.n_pages = 1;
+            d.scale = scale;
+            d.qk = qks ? &qks[i] : nullptr;
+            d.step = g->dev[b] + i;
+            d.grid = g->grid;
+            gkv::NewPages none{};
+            e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, none, t->scratch, d, t->num_sms, cs);
+        }
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e2 = cudaStreamEndCapture(cs, &graph);
+        if (e == cudaSuccess) e = e2;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&g->exec[b], graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+    }
+    if (e != cudaSuccess) st = cuda_fail(e, "decode step capture");
+    cudaStreamDestroy(cs);
+    return st;
+}
+
+}  // namespace
+
+int gkv_decode_graph_create(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids, const void* const* Q,
+                            const void* const* K, const void* const* V, void* const* out, int32_t n_q_heads,
+                            float scale, int32_t out_dtype, const gkv_qk_norm* const* qk, gkv_decode_graph** out_g) {
+    if (!out_g) return fail(GKV_ERR_INVALID, "gkv_decode_graph_create: null output");
+    *out_g = nullptr;
+    if (!m || n_layers < 1 || !layer_ids || !Q || !K || !V || !out)
+        return fail(GKV_ERR_INVALID, "gkv_decode_graph_create: bad arguments");
+    if (!is_out_dtype(out_dtype)) return fail(GKV_ERR_UNSUPPORTED, "out dtype %d", out_dtype);
+    std::vector<gkv::QkNorm> qks;
+    auto* g = new gkv_decode_graph();
+    g->m = m;
+    g->device = m->device;
+    g->n_q_heads = n_q_heads;
+    for (int32_t i = 0; i < n_layers; ++i) {
+        Layer* L = nullptr;
+        int st = ready_layer(m, layer_ids[i], &L);
+        if (!st && (L->n_kv_heads > 8 || L->head_dim != 128 || L->dtype != GKV_BF16))
+            st = fail(GKV_ERR_UNSUPPORTED, "layer %d: the decode kernel is built for head_dim 128, bf16, <= 8 kv heads",
+                      layer_ids[i]);
+        const int G = L && L->n_kv_heads ? n_q_heads / L->n_kv_heads : 0;
+        if (!st && (n_q_heads % L->n_kv_heads || (G != 1 && G != 2 && G != 4 && G != 8)))
+            st = fail(GKV_ERR_UNSUPPORTED, "n_q_heads %d over %d kv heads", n_q_heads, L->n_kv_heads);
+        for (int32_t j = 0; !st && j < i; ++j)
+            if (layer_ids[j] == layer_ids[i]) st = fail(GKV_ERR_INVALID, "layer %d listed twice", layer_ids[i]);
+        if (!st && (!Q[i] || !K[i] || !V[i] || !out[i] || !aligned16(Q[i]) || !aligned16(K[i]) || !aligned16(V[i]) ||
+                    !aligned16(out[i])))
+            st = fail(GKV_ERR_INVALID, "layer %d: Q/K/V/out must be non-null and 16-byte aligned", layer_ids[i]);
+        if (!st && qk && qk[i]) {
+            if ((st = check_qk(qk[i], 0, 1))) {
+            } else {
+                qks.push_back(gkv::QkNorm{qk[i]->q_norm_w, qk[i]->k_norm_w, qk[i]->cos_tab, qk[i]->sin_tab, qk[i]->eps});
+            }
+        } else if (!st && qk) {
+            st = fail(GKV_ERR_INVALID, "qk given for some layers only");
+        }
+        if (st) {
+            delete g;
+            return st;
+        }
+        g->layers.push_back(layer_ids[i]);
+        g->max_seq.push_back(qk ? qk[i]->max_seq : 0);
+    }
+    DeviceGuard dg(m->device);
+    if (!dg.ok()) {
+        delete g;
+        return fail(GKV_ERR_CUDA, "cannot select device %d", m->device);
+    }
+    int num_sms = 148;
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, g->device);
+    g->grid = std::min(num_sms, (int)(gkv::kMaxPartialRows / n_q_heads));
+    for (int32_t i = 0; i < n_layers; ++i) {
+        Layer* L = find_layer(m, layer_ids[i]);
+        gkv_pool_desc pool = pool_of(*L);
+        int st = table_maps(L->table, &pool);
+        if (st) {
+            decode_graph_free(g);
+            return st;
+        }
+    }
+    const size_t bytes = sizeof(gkv::DeviceStep) * n_layers;
+    if (cudaError_t e = gkv::configure_decode_kernels(); e != cudaSuccess) {  // not during capture
+        decode_graph_free(g);
+        return cuda_fail(e, "decode kernel attributes");
+    }
+    for (int b = 0; b < 2; ++b) {
+        cudaError_t e = cudaMallocHost(&g->host[b], bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&g->dev[b], bytes);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&g->done[b], cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            decode_graph_free(g);
+            return cuda_fail(e, "decode graph buffers");
+        }
+        memset(g->host[b], 0, bytes);
+        int st = capture_decode_graph(g, b, Q, K, V, out, n_q_heads, scale, out_dtype, qk ? qks.data() : nullptr);
+        if (st) {
+            decode_graph_free(g);
+            return st;
+        }
+    }
+    *out_g = g;
+    return GKV_OK;
+}
+
+int gkv_decode_graph_step(gkv_decode_graph* g, gkv_stream_t stream) {
+    if (!g) return fail(GKV_ERR_INVALID, "null decode graph");
+    DeviceGuard dg(g->device);
+    if (!dg.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", g->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int b = static_cast<int>(g->steps & 1);
+    // The pinned block b was last read by the step launched two steps ago.
+    if (g->launched[b]) {
+        cudaError_t e = cudaEventSynchronize(g->done[b]);
+        if (e != cudaSuccess) return cuda_fail(e, "decode graph: wait for the step block");
+    }
+    const size_t n = g->layers.size();
+    std::vector<int32_t> first(n, -1);
+    int st = GKV_OK;
+    size_t i = 0;
+    for (; i < n; ++i) {
+        Layer* L = nullptr;
+        if ((st = ready_layer(g->m, g->layers[i], &L))) break;
+        if (g->max_seq[i] && L->num_cached + 1 > g->max_seq[i]) {
+            st = fail(GKV_ERR_INVALID, "layer %d: position %d exceeds the RoPE table (%d rows)", g->layers[i],
+                      L->num_cached, g->max_seq[i]);
+            break;
+        }
+        int32_t f = 0, nn = 0;
+        if ((st = grow(*L, 1, &f, &nn))) break;
+        first[i] = f;
+        gkv_pool_desc pool = pool_of(*L);
+        gkv_new_pages np = pending(*L);
+        const int32_t total = L->num_cached + 1;
+        const int32_t n_pages = (total + 15) / 16;
+        if ((st = check_new_pages(L->table, &np, n_pages, pool.pool_pages))) break;
+        // Host-only growth beyond this step's page goes out first.
+        if (np.n_new_pages > 1 && (st = publish(&pool, L->table, &np, 0, np.n_new_pages - 1, s))) break;
+        gkv::DeviceStep& d = g->host[b][i];
+        d.n_prior = L->num_cached;
+        d.total = total;
+        d.n_pages = n_pages;
+        d.new_n = np.n_new_pages > 0 ? 1 : 0;
+        d.new_first = np.first_new_page + np.n_new_pages - 1;
+        d.new_id = d.new_n ? make_int2(np.k_ids[np.n_new_pages - 1], np.v_ids[np.n_new_pages - 1]) : make_int2(0, 0);
+        d.pad = 0;
+        if (!gkv::decode_split_geometry(n_pages, L->n_kv_heads, g->n_q_heads, 0, L->table->num_sms, &d.pages_per_split,
+                                        &d.n_splits) ||
+            d.n_splits > g->grid) {
+            st = fail(GKV_ERR_UNSUPPORTED, "layer %d: %d tokens need more splits than the captured grid (%d)",
+                      g->layers[i], total, g->grid);
+            break;
+        }
+    }
+    if (st) {
+        for (size_t j = 0; j <= i && j < n; ++j)
+            if (first[j] >= 0) ungrow(*find_layer(g->m, g->layers[j]), first[j]);
+        return st;
+    }
+    cudaError_t e = cudaGraphLaunch(g->exec[b], s);
+    if (e == cudaSuccess) e = cudaEventRecord(g->done[b], s);
+    if (e != cudaSuccess) {
+        for (size_t j = 0; j < n; ++j) ungrow(*find_layer(g->m, g->layers[j]), first[j]);
+        return cuda_fail(e, "decode graph launch");
+    }
+    g->launched[b] = true;
+    ++g->steps;
+    for (size_t j = 0; j < n; ++j) {
+        Layer* L = find_layer(g->m, g->layers[j]);
+        L->on_device = static_cast<int32_t>(L->k_ids.size());
+        L->num_cached += 1;
+    }
+    return GKV_OK;
+}
+
+int gkv_decode_graph_destroy(gkv_decode_graph* g) {
+    decode_graph_free(g);
+    return GKV_OK;
+}
+
 int gkv_export_kv(gkv_manager* m, int32_t layer_id, int32_t format, void* K_out, void* V_out, float* k_scales,
                   float* v_scales, int32_t* n_tokens, gkv_stream_t stream) {
     Layer* L = nullptr;

@@ -46,6 +46,22 @@ struct QkNorm {
     float eps;
 };
 
+// Per-step state of one layer's decode launch, in device memory: a captured
+// (CUDA-graph) decode step reads it instead of its launch parameters, which
+// are frozen at capture. The step's first node copies the host's values in;
+// the kernels only read it.
+struct DeviceStep {
+    int32_t n_prior;
+    int32_t total;
+    int32_t n_pages;
+    int32_t pages_per_split;
+    int32_t n_splits;
+    int32_t new_first;
+    int32_t new_n;       // 0 or 1
+    int32_t pad;
+    int2 new_id;
+};
+
 struct DecodeLaunch {
     const uint16_t* q;      // [Hq][128]
     const uint16_t* k_new;  // [Hkv][128] token appended by this step (or null)
@@ -59,7 +75,19 @@ struct DecodeLaunch {
     float scale;
     int32_t n_splits;       // 0 = choose
     const QkNorm* qk;       // non-null: q / k_new are pre-norm; QK-norm + RoPE fused (position n_prior)
+    const DeviceStep* step = nullptr;  // non-null: n_prior / total / n_pages / split size / new page from here
+    int32_t grid = 0;                  // with step: the fixed decode grid (>= every step's n_splits)
 };
+
+// Split geometry of a decode step: pages per split and the number of splits
+// (grid size), as launch_decode chooses them. Returns false when the context
+// needs more partial rows than the scratch holds.
+// Shared-memory size / carveout attributes of the decode kernels on the
+// current device (once per device; launch_decode calls it too).
+cudaError_t configure_decode_kernels();
+
+bool decode_split_geometry(int32_t n_pages, int32_t n_kv_heads, int32_t n_q_heads, int32_t n_splits_hint,
+                           int num_sms, int32_t* pages_per_split, int32_t* n_splits);
 
 // Head all-gather fused into the split combine (multi-GPU KV-head sharding):
 // every rank's combine stores its query-head block into every rank's full

@@ -399,6 +399,44 @@ class DecodeStep:
                                       self._hq, self._scale, self._odt, _stream_handle(self.manager.device, stream)))
 
 
+class DecodeGraph(DecodeStep):
+    """:class:`DecodeStep` captured once as a CUDA graph (gkv_decode_graph_*):
+    each ``run()`` is one graph launch for all layers, with the step state
+    (cached lengths, page counts, split geometry, new page ids) copied to the
+    device by the graph's first node. Same results as DecodeStep. With
+    ``qk`` (one :class:`QkNorm` per layer) Q and K are the projections and
+    QK-norm + RoPE run inside the decode kernel."""
+
+    def __init__(self, manager: PagedAttentionManager, layer_ids, Qs, Ks, Vs, outs, n_q_heads: int,
+                 scale: Optional[float] = None, qk=None):
+        super().__init__(manager, layer_ids, Qs, Ks, Vs, outs, n_q_heads, scale)
+        qk_arr = None
+        if qk is not None:
+            self._qk = list(qk)
+            if len(self._qk) != self._n:
+                raise GkvError(_lib.GKV_ERR_INVALID, "one QkNorm per layer")
+            qk_arr = (C.POINTER(_lib.QkNormDesc) * self._n)(*[C.pointer(q.desc) for q in self._qk])
+        self._qk_arr = qk_arr
+        h = C.c_void_p()
+        check(lib().gkv_decode_graph_create(self.manager.handle, self._n, self._ids, self._q, self._k, self._v,
+                                            self._o, self._hq, self._scale, self._odt, qk_arr, C.byref(h)))
+        self.handle = h
+
+    def run(self, stream=None) -> None:
+        check(lib().gkv_decode_graph_step(self.handle, _stream_handle(self.manager.device, stream)))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().gkv_decode_graph_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, out: Optional[torch.Tensor] = None,
                     scale: Optional[float] = None, causal: bool = True, stream=None) -> torch.Tensor:
     """``FlashAttentionImpl<CUDA>::execute`` on torch tensors: Q [B, Hq, S, D],

@@ -355,6 +355,31 @@ int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_f
                                const void* v_flat, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
                                int32_t causal, int32_t out_dtype, const gkv_qk_norm* qk, gkv_stream_t stream);
 
+/* gkv_decode_layers' decode step captured once as a CUDA graph and replayed per
+ * token: one graph launch per step instead of two kernel launches per layer.
+ * The layers' Q/K/V/out pointers (and, if qk is non-NULL, each layer's
+ * QK-norm + RoPE parameters: Q/K are then the projections, as
+ * gkv_paged_attention_qknorm takes them) are bound at creation. Each
+ * gkv_decode_graph_step allocates the step's pages on the host as
+ * gkv_decode_layers does, writes every layer's step state (cached length,
+ * page count, split geometry, new page id) into a pinned block, and launches
+ * the graph, whose first node copies that block to the device; the kernels
+ * read it there instead of their frozen launch parameters. Results are
+ * identical to gkv_decode_layers (same kernels, same split geometry). The
+ * decode grid is fixed at one CTA per SM, which bounds the context a step
+ * can serve (GKV_ERR_UNSUPPORTED beyond it; 147 splits of up to 1000 pages).
+ * A step waits on the host only for the step launched two steps earlier to
+ * finish (the pinned blocks alternate). Not for the multi-GPU gather tier.
+ * The step's layers must not be driven by other calls while the graph is in
+ * use, except between steps on the same stream. */
+typedef struct gkv_decode_graph gkv_decode_graph;
+int gkv_decode_graph_create(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids, const void* const* Q,
+                            const void* const* K, const void* const* V, void* const* out, int32_t n_q_heads,
+                            float scale, int32_t out_dtype, const gkv_qk_norm* const* qk,
+                            gkv_decode_graph** graph);
+int gkv_decode_graph_step(gkv_decode_graph* graph, gkv_stream_t stream);
+int gkv_decode_graph_destroy(gkv_decode_graph* graph);
+
 /* ---------------- non-paged attention ------------------------------------
  * FlashAttentionImpl<CUDA>::execute (src/backend/cuda/attention.cu:317-399;
  * semantics of the CPU op, src/backend/cpu/attention.cpp:39-120):

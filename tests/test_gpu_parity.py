@@ -277,6 +277,8 @@ def test_config4_chunked_prefill_qwen3_1p7b():
     m = PagedAttentionManager(0)
     m.init_layer(0, hkv, d)
     m.reserve_layer(0, pool_pages)
+    for t in m.pool_tensors(0):  # fresh device memory is not zeroed; the restated pools are
+        t.zero_()
     op = OraclePool(pool_pages, ORC)
     kp = np.zeros((pool_pages, 16, hkv, d), np.uint16)
     vp = np.zeros((pool_pages, 16, hkv, d), np.uint16)
