@@ -715,6 +715,15 @@ def main():
             if world > 1:
                 allgather_heads(wl.layers[l].out, gathered[l])
 
+    # One GPU: the same step is also captured as a CUDA graph
+    # (gkv_decode_graph_step: host page allocation + one graph launch),
+    # timed separately below. The headline keeps one call per layer.
+    graph = None
+    if hg is None and world == 1:
+        from genllm_b200.paged_attention import DecodeGraph
+        graph = DecodeGraph(wl.mgr, list(range(args.layers)), [b.q for b in wl.layers], [b.k for b in wl.layers],
+                            [b.v for b in wl.layers], [b.out for b in wl.layers], wl.hq_local, wl.scale)
+
     def step(events=None):
         for l in range(args.layers):
             if events is not None:
@@ -745,6 +754,30 @@ def main():
     if world > 1:
         dist.barrier()
     ms = t_start.elapsed_time(t_end)
+    captured = None
+    if graph is not None:
+        # The same steps through the captured multi-layer step: the layers are
+        # distinct and their inputs ready before the step, so each combine
+        # releases the next layer's decode at entry and the layers after the
+        # first do not wait for their predecessor before computing.
+        for _ in range(args.warmup):
+            graph.run()
+        torch.cuda.synchronize()
+        ctx_g = wl.cached(0)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            graph.run()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = g0.elapsed_time(g1)
+        g_bytes = sum(args.layers * wl.bytes_per_layer_token(ctx_g + k + 1) for k in range(args.steps))
+        captured = {"value": round(g_bytes / (g_ms / 1e3) / 1e9, 2), "unit": UNIT,
+                    "ms_per_step": round(g_ms / args.steps, 4),
+                    "us_per_token_layer": round(1e3 * g_ms / (args.steps * args.layers), 3),
+                    "path": "gkv_decode_graph_step: the 36 layers' decode + combine kernels replayed from one CUDA "
+                            "graph; combines release the next layer's decode at entry, layers after the first "
+                            "skip the wait on their predecessor (their inputs were ready before the step)"}
     # Per-launch device time of one layer's decode step (decode + combine
     # kernels), from CUDA events around each call on the launching stream in a
     # separate instrumented pass (events between launches serialise them).
@@ -787,15 +820,14 @@ def main():
     h_in.copy_(wl.inbuf)
     h_out = torch.empty((args.layers, (HQ if world > 1 else hq_l) * D), dtype=torch.bfloat16).pin_memory()
 
-    from genllm_b200.paged_attention import DecodeGraph, DecodeStep
-    one_call = graph = None
-    if hg is None and world == 1:
-        # The whole step's 36 layers through one library call, and the same
-        # step captured as a CUDA graph (one graph launch per step).
+    from genllm_b200.paged_attention import DecodeStep
+    one_call = None
+    if graph is not None:
+        # The whole step's 36 layers through one library call, beside the
+        # captured step (one graph launch per step).
         bound = ([b.q for b in wl.layers], [b.k for b in wl.layers], [b.v for b in wl.layers],
                  [b.out for b in wl.layers])
         one_call = DecodeStep(wl.mgr, list(range(args.layers)), *bound, hq_l, wl.scale)
-        graph = DecodeGraph(wl.mgr, list(range(args.layers)), *bound, hq_l, wl.scale)
     enqueue = [0.0]
 
     def e2e_step(runner=None):
@@ -807,6 +839,7 @@ def main():
             h_out.copy_(wl.outbuf, non_blocking=True)
             torch.cuda.current_stream().synchronize()
             return float(h_out[-1, 0])
+        h0 = time.perf_counter()
         for l in range(args.layers):
             L = wl.layers[l]
             if hg is not None:
@@ -815,6 +848,7 @@ def main():
                 paged_attention(wl.mgr, l, L.q, L.k, L.v, out=L.out, scale=wl.scale)
                 if world > 1:
                     allgather_heads(L.out, gathered[l])
+        enqueue[0] += time.perf_counter() - h0
         h_out.copy_(gathered_all if world > 1 else wl.outbuf, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         return float(h_out[-1, 0])  # the step's result, read on the host
@@ -845,19 +879,18 @@ def main():
         return be.item() / (te.item() / 1e3) / 1e9, te.item() / e2e_steps, 1e3 * enqueue[0] / e2e_steps
 
     extra_e2e = {}
+    e2e_value, e2e_ms, e2e_enq = e2e_run(None)
+    e2e_path = ("one pinned H2D copy of all layers Q/K/V, per-layer C ABI calls, one D2H copy of the "
+                "outputs, host reads the result")
     if graph is not None:
         v1, ms1, enq1 = e2e_run(one_call)
+        v2, ms2, enq2 = e2e_run(graph)
         extra_e2e = {"one_call": {"value": round(v1, 2), "ms_per_step": round(ms1, 4),
                                   "host_call_ms_per_step": round(enq1, 4),
-                                  "path": "same copies, one gkv_decode_layers call per step"}}
-        e2e_value, e2e_ms, e2e_enq = e2e_run(graph)
-        e2e_path = ("one pinned H2D copy of all layers Q/K/V, one gkv_decode_graph_step call (C ABI: host page "
-                    "allocation + one CUDA-graph launch of the 36 layers' kernels), one D2H copy of the outputs, "
-                    "host reads the result")
-    else:
-        e2e_value, e2e_ms, e2e_enq = e2e_run(None)
-        e2e_path = ("one pinned H2D copy of all layers Q/K/V, per-layer C ABI calls, one D2H copy of the "
-                    "outputs, host reads the result")
+                                  "path": "same copies, one gkv_decode_layers call per step"},
+                     "captured_step": {"value": round(v2, 2), "ms_per_step": round(ms2, 4),
+                                       "host_call_ms_per_step": round(enq2, 4),
+                                       "path": "same copies, one gkv_decode_graph_step call per step"}}
     h2d = h_in.numel() * 2
     d2h = h_out.numel() * 2
 
@@ -883,6 +916,8 @@ def main():
         "gpu_launches": 2 * args.steps * args.layers,
         "gather": (args.gather if world > 1 else None),
         "host_enqueue_ms_per_step": round(1e3 * host_enqueue_s / args.steps, 4),
+        "timed_path": "per-layer C ABI calls (decode + combine kernels each), one call per layer",
+        "captured_step": captured,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args, world),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of paged_decode_kernel "

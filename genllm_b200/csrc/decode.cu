@@ -81,6 +81,7 @@ struct DecodeParams {
     int32_t qk_on;  // 1: q / k_new are pre-norm projections: QK-norm + RoPE here (position n_prior)
     QkNorm qk;
     const DeviceStep* step;  // non-null: the step fields above come from here (captured steps)
+    int32_t inputs_ready;    // 1: previous launch is another layer's combine of the same step (see kernel)
     float qscale;  // softmax scale * log2(e)
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
@@ -259,7 +260,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             const size_t pos = (size_t)sf.n_prior * kHeadDim;
             rq = load_row_params_g8(a.qk.q_w, a.qk.cos + pos, a.qk.sin + pos, lane & 7);
         }
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // Inside a multi-layer step whose layers are distinct, the layers
+        // after the first read inputs that were complete before the step's
+        // first launch: no wait here (one thread waits at the end instead, so
+        // that this grid still completes after the previous kernel).
+        if (!a.inputs_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
         PROBE_T(5);
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
         uint32_t qb[8][2];
@@ -545,6 +550,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();
     PROBE_T(3);
+    if (a.inputs_ready && threadIdx.x == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 
 #ifdef GKV_PROBE_TIMELINE
     __syncthreads();
@@ -562,6 +568,7 @@ struct CombineParams {
     uint32_t* err;
     GatherLaunch g;
     const DeviceStep* step;  // non-null: n_splits from here (captured steps)
+    int32_t early;           // 1: the next launch is another layer's decode: trigger it at entry
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
 #endif
@@ -580,14 +587,20 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
 #define PROBE_C(k)
 #endif
     PROBE_C(0);
+    // When the next launch is another layer's decode (a multi-layer step
+    // whose layers are distinct, and not its last layer), it reads nothing
+    // this layer's grids write before its own wait: it may start now, its
+    // page stream overlapping this layer's tail.
+    const bool gather = c.g.world > 1;
+    if (c.early && !gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
     PROBE_C(1);
-    // Only now may the next launch start: a decode step of the same layer
-    // reads pages and table entries this step's decode grid wrote, and its
-    // page stream begins before it waits for this grid. With the fused
-    // gather the trigger comes after this rank's stores and flags are out.
-    const bool gather = c.g.world > 1;
-    if (!gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Otherwise only now may the next launch start: a decode step of the
+    // same layer reads pages and table entries this step's decode grid
+    // wrote, and its page stream begins before it waits for this grid. With
+    // the fused gather the trigger comes after this rank's stores and flags
+    // are out.
+    if (!c.early && !gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int hq = blockIdx.x;
     const int lane = threadIdx.x & 31;
     const int d = blockIdx.y * kCombineDims + lane;
@@ -783,6 +796,7 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     if (!decode_split_geometry(d.n_pages, Hkv, d.n_q_heads, d.n_splits, num_sms, &p.pages_per_split, &n_splits))
         return cudaErrorInvalidValue;
     p.step = d.step;
+    p.inputs_ready = d.prev_is_other_layer ? 1 : 0;
     int grid = n_splits;
     if (d.step) {
         // Captured step: the geometry in the step block changes from token
@@ -812,6 +826,7 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits, scratch.err, {}};
     if (gather) c.g = *gather;
     c.step = d.step;
+    c.early = d.next_is_other_layer ? 1 : 0;
 #ifdef GKV_PROBE_TIMELINE
     c.probe_slot = p.probe_slot;
 #endif

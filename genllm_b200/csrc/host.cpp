@@ -38,6 +38,10 @@ thread_local std::string g_last_error;
 // Set by gkv_paged_attention_gather around its call of the managed decode
 // path: the fused head all-gather of that one launch.
 thread_local const gkv::GatherLaunch* t_gather = nullptr;
+// Set by the multi-layer entry points around every layer but the last of a
+// step whose layers are distinct: the next launch is another layer's decode.
+thread_local bool t_next_other_layer = false;
+thread_local bool t_prev_other_layer = false;  // ... and around every layer but the first
 
 int fail(int status, const char* fmt, ...) {
     char buf[512];
@@ -533,6 +537,8 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
         d.scale = scale;
         d.n_splits = 0;
         d.qk = qk;
+        d.next_is_other_layer = t_next_other_layer;
+        d.prev_is_other_layer = t_prev_other_layer;
         cudaError_t e =
             gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s, t_gather);
         if (e != cudaSuccess) return cuda_fail(e, "decode launch");
@@ -1017,13 +1023,23 @@ int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids
                       int32_t out_dtype, gkv_stream_t stream) {
     if (!m || n_layers < 0 || (n_layers && (!layer_ids || !Q || !K || !V || !out)))
         return fail(GKV_ERR_INVALID, "gkv_decode_layers: bad arguments");
+    bool distinct = true;
+    for (int32_t i = 0; i < n_layers && distinct; ++i)
+        for (int32_t j = 0; j < i; ++j)
+            if (layer_ids[j] == layer_ids[i]) distinct = false;
     for (int32_t i = 0; i < n_layers; ++i) {
         Layer* L = nullptr;
         int st = ready_layer(m, layer_ids[i], &L);
         if (st) return st;
         if (n_q_heads % L->n_kv_heads) return fail(GKV_ERR_INVALID, "n_q_heads %d, n_kv_heads %d", n_q_heads, L->n_kv_heads);
+        // A layer whose new pages exceed one launch's list publishes them
+        // with extra launches first, which breaks the chain of early releases.
+        const int32_t pend = static_cast<int32_t>(L->k_ids.size()) - L->on_device + 1;
+        t_next_other_layer = distinct && i + 1 < n_layers;
+        t_prev_other_layer = distinct && i > 0 && pend <= gkv::kMaxNewPagesPerLaunch;
         st = gkv_paged_attention(m, layer_ids[i], Q[i], K[i], V[i], out[i], 1, n_q_heads, 1, L->head_dim,
                                  L->n_kv_heads, scale, 1, n_q_heads / L->n_kv_heads, L->dtype, out_dtype, stream);
+        t_next_other_layer = t_prev_other_layer = false;
         if (st) return st;
     }
     return GKV_OK;
@@ -1095,6 +1111,8 @@ int capture_decode_graph(gkv_decode_graph* g, int b, const void* const* Q, const
             d.qk = qks ? &qks[i] : nullptr;
             d.step = g->dev[b] + i;
             d.grid = g->grid;
+            d.next_is_other_layer = i + 1 < n;  // the graph's layers are distinct
+            d.prev_is_other_layer = i > 0;
             gkv::NewPages none{};
             e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, none, t->scratch, d, t->num_sms, cs);
         }

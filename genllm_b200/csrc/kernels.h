@@ -77,6 +77,12 @@ struct DecodeLaunch {
     const QkNorm* qk;       // non-null: q / k_new are pre-norm; QK-norm + RoPE fused (position n_prior)
     const DeviceStep* step = nullptr;  // non-null: n_prior / total / n_pages / split size / new page from here
     int32_t grid = 0;                  // with step: the fixed decode grid (>= every step's n_splits)
+    bool next_is_other_layer = false;  // the next launch on the stream is a decode of a layer distinct
+                                       // from this one and from every layer launched since the last
+                                       // launch without this flag: the combine releases it at entry
+    bool prev_is_other_layer = false;  // the previous launch is the combine of an earlier layer of the
+                                       // same multi-layer step (launched with next_is_other_layer), and
+                                       // Q / K / V were complete before the step's first launch
 };
 
 // Split geometry of a decode step: pages per split and the number of splits
