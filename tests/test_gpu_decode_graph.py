@@ -160,3 +160,48 @@ def test_graph_step_fails_whole_when_a_pool_runs_out():
     torch.cuda.synchronize()
     assert ma.check_device_errors(0) == 0 and ma.check_device_errors(1) == 0
     graph.close()
+
+
+@pytest.mark.parametrize("runner", ["graph", "one_call"])
+def test_multi_layer_steps_back_to_back_match_per_layer_calls(runner):
+    """Thirty steps of a four-layer step (early release between layers) with
+    no host synchronisation between steps, against per-layer calls (each
+    launch ordered after the previous one): every step's outputs and the
+    final pages bit-identical. Contexts of very different lengths make the
+    layers' grids end unevenly."""
+    priors = [2000, 17, 3000, 500]
+    cases, ma, mb = twin_managers(priors, 3000 // 16 + 8, seed=21)
+    dev = ma.device
+    n, steps = len(priors), 30
+    qa, ka, va, oa = bound_tensors(n, dev)
+    g = torch.Generator(device=dev).manual_seed(12)
+    feed_q = torch.randn((steps, n, HQ, 128), generator=g, device=dev).to(torch.bfloat16)
+    feed_k = torch.randn((steps, n, HKV, 128), generator=g, device=dev).to(torch.bfloat16)
+    feed_v = torch.randn((steps, n, HKV, 128), generator=g, device=dev).to(torch.bfloat16)
+    hist_a = torch.empty((steps, n, HQ, 128), dtype=torch.bfloat16, device=dev)
+    hist_b = torch.empty_like(hist_a)
+    r = (DecodeGraph if runner == "graph" else DecodeStep)(ma, list(range(n)), qa, ka, va, oa, HQ)
+    torch.cuda.synchronize()
+    for t in range(steps):
+        for l in range(n):
+            qa[l].copy_(feed_q[t, l])
+            ka[l].copy_(feed_k[t, l])
+            va[l].copy_(feed_v[t, l])
+        r.run()
+        for l in range(n):
+            hist_a[t, l].copy_(oa[l])
+    from genllm_b200.paged_attention import paged_attention
+    ob = torch.empty((1, HQ, 1, 128), dtype=torch.bfloat16, device=dev)
+    for t in range(steps):
+        for l in range(n):
+            paged_attention(mb, l, feed_q[t, l].view(1, HQ, 1, 128), feed_k[t, l].view(1, HKV, 1, 128),
+                            feed_v[t, l].view(1, HKV, 1, 128), out=ob)
+            hist_b[t, l].copy_(ob[0, :, 0])
+    torch.cuda.synchronize()
+    assert torch.equal(hist_a, hist_b)
+    for l in range(n):
+        assert torch.equal(ma.pool_tensors(l)[0], mb.pool_tensors(l)[0])
+        assert torch.equal(ma.pool_tensors(l)[1], mb.pool_tensors(l)[1])
+        assert ma.check_device_errors(l) == 0
+    if runner == "graph":
+        r.close()
