@@ -1032,10 +1032,14 @@ int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids
         int st = ready_layer(m, layer_ids[i], &L);
         if (st) return st;
         if (n_q_heads % L->n_kv_heads) return fail(GKV_ERR_INVALID, "n_q_heads %d, n_kv_heads %d", n_q_heads, L->n_kv_heads);
-        // A layer whose new pages exceed one launch's list publishes them
-        // with extra launches first, which breaks the chain of early releases.
+        // Layer 0's combine releases layer 1 only after layer 0's decode has
+        // completed, i.e. after its wait on whatever produced the step's
+        // inputs (a kernel before this call may itself release early); from
+        // there on the inputs are complete and the layers distinct. A layer
+        // whose new pages exceed one launch's list publishes them with extra
+        // launches first: it keeps the wait.
         const int32_t pend = static_cast<int32_t>(L->k_ids.size()) - L->on_device + 1;
-        t_next_other_layer = distinct && i + 1 < n_layers;
+        t_next_other_layer = distinct && i >= 1 && i + 1 < n_layers;
         t_prev_other_layer = distinct && i > 0 && pend <= gkv::kMaxNewPagesPerLaunch;
         st = gkv_paged_attention(m, layer_ids[i], Q[i], K[i], V[i], out[i], 1, n_q_heads, 1, L->head_dim,
                                  L->n_kv_heads, scale, 1, n_q_heads / L->n_kv_heads, L->dtype, out_dtype, stream);
@@ -1111,7 +1115,10 @@ int capture_decode_graph(gkv_decode_graph* g, int b, const void* const* Q, const
             d.qk = qks ? &qks[i] : nullptr;
             d.step = g->dev[b] + i;
             d.grid = g->grid;
-            d.next_is_other_layer = i + 1 < n;  // the graph's layers are distinct
+            // The graph's layers are distinct, and its first node (the copy)
+            // runs after all earlier work on the stream has completed, so the
+            // inputs are complete when layer 0's decode starts.
+            d.next_is_other_layer = i + 1 < n;
             d.prev_is_other_layer = i > 0;
             gkv::NewPages none{};
             e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, none, t->scratch, d, t->num_sms, cs);
