@@ -71,3 +71,22 @@ def test_kv_format_entry_points_reject_bad_arguments_without_a_gpu():
     assert L.gkv_export_kv(m, 0, 0, None, None, None, None, C.byref(n), None) == _lib.GKV_ERR_STATE
     assert L.gkv_import_kv(m, 0, 1, None, None, None, None, 4, None) == _lib.GKV_ERR_STATE
     assert L.gkv_manager_destroy(m) == 0
+
+
+def test_decode_graph_entry_points_reject_bad_arguments_without_a_gpu():
+    import ctypes as C
+    L = _lib.lib()
+    g = C.c_void_p()
+    assert L.gkv_decode_graph_create(None, 1, None, None, None, None, None, 8, 0.1, 30, None, C.byref(g)) == \
+        _lib.GKV_ERR_INVALID
+    assert L.gkv_decode_graph_step(None, None) == _lib.GKV_ERR_INVALID
+    assert L.gkv_decode_graph_destroy(None) == 0
+    m = C.c_void_p()
+    assert L.gkv_manager_create(-1, C.byref(m)) == 0
+    assert L.gkv_init_layer(m, 0, 8, 128, _lib.GKV_BF16) == 0
+    ids = (C.c_int32 * 1)(0)
+    ptrs = (C.c_void_p * 1)(16)
+    # a host-only manager has no device pools to capture
+    assert L.gkv_decode_graph_create(m, 1, ids, ptrs, ptrs, ptrs, ptrs, 8, 0.1, 30, None, C.byref(g)) == \
+        _lib.GKV_ERR_STATE
+    assert L.gkv_manager_destroy(m) == 0
