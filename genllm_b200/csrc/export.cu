@@ -15,11 +15,15 @@
 //                                               values saturate at +-448, NaN -> 0x7F)
 //   x'    = bf16(e4m3_value(q) * scale)        (import: the reference's bf16 rounding)
 //
-// One warp per (K|V, page, head) unit for the export: it reads the unit's 16
-// rows of 256 bytes (two slots per load instruction, 8 loads in flight per
-// lane), reduces the block's amax with shuffles, and writes the 16 rows of
-// the head-major output, which are contiguous. Both directions are a single
-// pass over HBM: read 2 B and write 1 B (fp8) or 2 B (bf16) per element.
+// One warp per (K|V, page, head) unit for the export: it copies the unit's
+// 16 rows of 256 bytes into its shared-memory ring with cp.async (two slots
+// per instruction), kRing - 1 units ahead of the one it converts; reduces the
+// block's amax with shuffles, and writes the 16 rows of the head-major
+// output, which are contiguous. The import is the same with one warp per
+// (K|V, 16-token block, head). Both directions are a single pass over HBM:
+// read 2 B and write 1 B (fp8) or 2 B (bf16) per element. The hardware
+// conversions are used only where they give the rounding defined above
+// bit for bit (see each kernel); elsewhere the element-wise path runs.
 #include <atomic>
 
 #include "device.cuh"
@@ -287,8 +291,8 @@ __device__ __forceinline__ float2 e4m3x2_to_f32(uint32_t b) {
 
 // One warp per (K|V, 16-token input block, head) unit: each half-warp reads a
 // token's 128-byte e4m3 row (8 bytes a lane) and writes its 256-byte page row
-// (16 bytes a lane); 8 rows per lane, the next unit's loads issued before the
-// current unit is converted and stored.
+// (16 bytes a lane); 8 rows per lane, kRing - 1 units' copies in flight in
+// the warp's shared-memory ring while the current unit is converted.
 struct ImportUnit {
     const uint2* src;  // this lane's first 8-byte unit
     float scale;
