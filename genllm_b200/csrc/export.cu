@@ -265,6 +265,36 @@ __global__ void __launch_bounds__(256, 2) kv_export_kernel(const ExportParams a)
     cp_async_wait<0>();
 }
 
+// The bf16 export is a byte copy: no ring, few registers, many warps. One
+// warp per (K|V, page, head) unit, 8 x 16 bytes in flight per lane.
+__global__ void __launch_bounds__(256, 4) kv_export_bf16_kernel(const ExportParams a) {
+    constexpr int kUnitsPerRow = kHeadDim * 2 / 16;
+    const int lane = threadIdx.x & 31;
+    const int half = lane >> 4;
+    const int col = lane & 15;
+    const long long units = 2ll * a.n_pages * a.n_kv_heads;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long u = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
+        const ExportUnit x = export_unit(a, u, half, col);
+        if (!x.src) {
+            if (lane == 0) atomicOr(a.err, kErrBadPage);
+            continue;
+        }
+        uint4 v[kPageSlots / 2];
+#pragma unroll
+        for (int i = 0; i < kPageSlots / 2; ++i) {
+            const int slot = 2 * i + half;
+            if (slot < x.valid) v[i] = __ldcs(x.src + (size_t)slot * a.n_kv_heads * kUnitsPerRow);
+        }
+        uint4* dst = static_cast<uint4*>(x.which ? a.v_out : a.k_out) + x.row0 * kUnitsPerRow + col;
+#pragma unroll
+        for (int i = 0; i < kPageSlots / 2; ++i) {
+            const int slot = 2 * i + half;
+            if (slot < x.valid) __stcs(dst + (size_t)slot * kUnitsPerRow, v[i]);
+        }
+    }
+}
+
 struct ImportParams {
     const uint2* k_in;  // [Hkv][seq_len][128] e4m3
     const uint2* v_in;
@@ -435,6 +465,10 @@ cudaError_t launch_export(const PoolView& pool, const int2* table, int32_t n_tok
     a.pool_pages = pool.pool_pages;
     a.fp8 = fp8;
     const long long units = 2ll * a.n_pages * pool.n_kv_heads;
+    if (!fp8) {
+        kv_export_bf16_kernel<<<(unsigned)grid_for(units, 8, num_sms, 4), 256, 0, stream>>>(a);
+        return cudaGetLastError();
+    }
     constexpr int smem = 8 * kRing * kPageSlots * kHeadDim * 2;  // 8 warps x kRing x 4 KiB
     static std::atomic<uint64_t> configured{0};  // devices whose attribute is set
     int dev = 0;
