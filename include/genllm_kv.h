@@ -130,7 +130,12 @@ int gkv_paged_attention(gkv_manager* m, int32_t layer_id, const void* Q, const v
  * this is a launch loop in the library: one host call per step instead of one
  * per layer, the executor's per-op host cost gone (the reference executor
  * synchronises the device after every op, src/core/executor.cpp:169-172).
- * Stops at the first failing layer (layers before it have advanced). */
+ * Every layer's Q, K and V must be complete when the call's first launch
+ * runs (produced by earlier work on the stream), and no layer's out may be
+ * another listed layer's Q, K or V: with distinct layers the kernels of
+ * layer i + 1 start while layer i finishes and read their inputs without
+ * waiting for it. Stops at the first failing layer (layers before it have
+ * advanced). */
 int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids, const void* const* Q,
                       const void* const* K, const void* const* V, void* const* out, int32_t n_q_heads,
                       float scale, int32_t out_dtype, gkv_stream_t stream);
@@ -365,7 +370,9 @@ int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_f
  * page count, split geometry, new page id) into a pinned block, and launches
  * the graph, whose first node copies that block to the device; the kernels
  * read it there instead of their frozen launch parameters. Results are
- * identical to gkv_decode_layers (same kernels, same split geometry). The
+ * identical to gkv_decode_layers (same kernels, same split geometry), with
+ * the same requirement on the inputs (complete before the step, no layer's
+ * out feeding another layer of the step). The
  * decode grid is fixed at one CTA per SM, which bounds the context a step
  * can serve (GKV_ERR_UNSUPPORTED beyond it; 147 splits of up to 1000 pages).
  * A step waits on the host only for the step launched two steps earlier to
