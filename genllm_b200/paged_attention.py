@@ -376,7 +376,10 @@ class DecodeStep:
     """One decode token through a fixed list of layers with one library call
     (gkv_decode_layers). The tensors are bound once: Q [Hq, 128] and K, V
     [Hkv, 128] per layer (any views of device memory), out [Hq, 128]; each
-    ``run()`` appends one token to every layer and attends."""
+    ``run()`` appends one token to every layer and attends. The layers are
+    independent: their inputs are complete before ``run()`` and no layer's
+    out is another's Q/K/V (layer i + 1's kernels start while layer i
+    finishes)."""
 
     def __init__(self, manager: PagedAttentionManager, layer_ids, Qs, Ks, Vs, outs, n_q_heads: int,
                  scale: Optional[float] = None):
