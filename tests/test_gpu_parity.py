@@ -80,6 +80,16 @@ def test_chunk_paths(n_prior, n_new, causal):
     check_case(case, causal)
 
 
+@pytest.mark.parametrize("g,hkv", [(1, 8), (4, 8), (8, 2), (8, 1), (2, 3), (1, 5)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_chunk_group_sizes(g, hkv, causal):
+    """The chunk path (tensor-core prefill) at every group size and at kv
+    head counts that are not a power of two, with the context ending mid-page."""
+    case = fragmented_case(400 + 10 * g + hkv, g * hkv, hkv, 128, 203, (203 + 150) // 16 + 5, n_new=150,
+                           poison_unused=True)
+    check_case(case, causal)
+
+
 def test_long_chunk_over_1024_tokens():
     """Chunks longer than one append launch carries (64 pages) are split."""
     case = fragmented_case(77, 4, 2, 128, 40, 200, n_new=1500)
