@@ -150,3 +150,32 @@ def test_import_at_an_offset_matches_append_of_dequantised_values():
     k_ids, v_ids = pool.table()
     ORC.import_fp8(kp, vp, k_ids, v_ids, n_prior, q[0], q[1], scales[0], scales[1])
     assert np.array_equal(kp, kp_a) and np.array_equal(vp, vp_a)
+
+
+def test_e4m3_encoder_is_nearest_even_by_brute_force():
+    """Independent of torch: for random fp32 inputs inside +-448 the code is
+    the nearest of all 255 finite e4m3 values, ties to the even code."""
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.uint8)
+    vals = ORC.e4m3_to_f32(codes).astype(np.float64)
+    rng = np.random.default_rng(9)
+    x = np.concatenate([rng.uniform(-448, 448, 3000), rng.standard_normal(3000) * 2.0 ** rng.integers(-12, 8, 3000),
+                        (vals[:, None] + vals[None, :]).ravel()[::7] / 2]).astype(np.float32)  # midpoints: ties
+    x = x[np.abs(x) <= 448]
+    got = ORC.e4m3_from_f32(x)
+    d = np.abs(vals[None, :] - x.astype(np.float64)[:, None])
+    best = d.min(axis=1)
+    for i in range(len(x)):
+        cand = codes[d[i] == best[i]]
+        if len(cand) == 1:
+            want = cand[0]
+        else:  # a tie: the even mantissa (for +-0, the code with x's sign)
+            even = [c for c in cand if (c & 1) == 0]
+            want = even[0] if len(even) == 1 else (0x80 if np.signbit(x[i]) else 0x00)
+        assert got[i] == want, (float(x[i]), int(got[i]), int(want))
+
+
+def test_e4m3_encoder_monotone_and_symmetric():
+    x = np.sort(np.random.default_rng(4).uniform(0, 500, 5000).astype(np.float32))
+    v = ORC.e4m3_to_f32(ORC.e4m3_from_f32(x))
+    assert (np.diff(v) >= 0).all()
+    assert np.array_equal(ORC.e4m3_from_f32(-x), ORC.e4m3_from_f32(x) | 0x80)
