@@ -1,4 +1,4 @@
-"""Benchmark of the paged KV-cache decode path (BASELINE config 3 / 5).
+"""Benchmark of the paged KV-cache decode path: Qwen3-4B layer-shape decode at 32k context (one GPU), and the same KV-head sharded over N GPUs.
 
 Workload: Qwen3-4B layer shape (Hq=32, Hkv=8, D=128, bf16), 36 layers, each
 with 32768 cached tokens in a fragmented block table over a 4096-page pool
@@ -735,6 +735,22 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # Self-check before timing: layer 0's output of the last warm-up step,
+    # gathered over the ranks, against a torch fp32 recomputation of all
+    # heads from the workload's seeded values (rank 0).
+    parity = None
+    if args.warmup > 0 and rank == 0:
+        got = (gathered_all[0] if world > 1 else wl.layers[0].out).float().reshape(HQ, D)
+        want = wl.reference_output(0)
+        err = (got - want).abs()
+        big = want.abs() >= 1e-3
+        max_abs = float(err.max())
+        max_rel = float((err[big] / want[big].abs()).max()) if bool(big.any()) else 0.0
+        parity = {"layer": 0, "max_abs": max_abs, "max_rel": max_rel, "ok": max_abs <= 2e-3 and max_rel <= 1e-2,
+                  "bounds": "max-abs 2e-3; max-rel 1e-2 over |want| >= 1e-3",
+                  "against": "torch fp32 recomputation of all heads from the seeded workload (bf16 output rounded)"}
+        del want, got, err
+        torch.cuda.empty_cache()
     ctx0 = wl.cached(0)
 
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -913,7 +929,7 @@ def main():
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps, "ms_per_step": round(e2e_ms, 4), "host_call_ms_per_step": round(e2e_enq, 4),
                 "path": e2e_path, **extra_e2e},
-        "gpu_launches": 2 * args.steps * args.layers,
+        "gpu_launches": (1 if os.environ.get("GKV_DECODE_FUSED_MERGE") == "1" and not (world > 1 and args.gather == "p2p") else 2) * args.steps * args.layers,
         "gather": (args.gather if world > 1 else None),
         "host_enqueue_ms_per_step": round(1e3 * host_enqueue_s / args.steps, 4),
         "timed_path": "per-layer C ABI calls (decode + combine kernels each), one call per layer",
@@ -930,6 +946,7 @@ def main():
                                            "how": "separate pass, CUDA events recorded between launches (no "
                                                   "overlap of consecutive launches)"}},
         "clocks": clk,
+        "parity": parity,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_step(args)  # warm-up (and set-up) step, untimed

@@ -89,9 +89,11 @@ SIGNATURES = {
     "gkv_ipc_close": ([C.c_int, vp], C.c_int),
     "gkv_gather_create": ([C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp)], C.c_int),
     "gkv_gather_destroy": ([vp], C.c_int),
+    "gkv_gather_set_wait_limit": ([vp, C.c_uint64], C.c_int),
     "gkv_paged_attention_gather": ([vp, i32, vp, vp, vp, vp, C.c_size_t, i32, C.c_float, i32, vp], C.c_int),
     "gkv_paged_decode_static_scratch": ([C.POINTER(PoolDesc), vp, i32, vp, vp, vp, vp, i32, C.c_float, i32, vp],
                                         C.c_int),
+    "gkv_paged_decode_static_scratch_errors": ([u32p, vp], C.c_int),
     "gkv_rope_cache": ([C.c_float, i32, i32, vp, vp], C.c_int),
     "gkv_flash_attention": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, C.c_float, i32, i32, i32, vp], C.c_int),
     "gkv_flash_check_errors": ([u32p], C.c_int),

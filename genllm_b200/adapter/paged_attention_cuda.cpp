@@ -16,8 +16,9 @@
 //   * append + attention run as one fused decode launch (+ the split
 //     combine) for seq_len == 1, or append + tensor-core prefill otherwise,
 //     instead of 2*Hkv*S synchronous cudaMemcpy calls and a serial kernel.
-// An exhausted pool throws instead of leaving num_cached ahead of the table
-// (src/core/page_attention.cpp:155,161).
+// An exhausted pool throws before any page is taken, instead of leaving
+// num_cached ahead of the table and popped ids unreachable
+// (src/core/page_attention.cpp:152-161).
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -42,6 +43,35 @@ struct DeviceMirror {
 
 std::mutex g_mu;
 std::map<std::pair<const PagedAttentionManager*, int32_t>, DeviceMirror> g_mirrors;
+
+// BlockPool keeps its capacity (the max_blocks reserve_layer carved) private
+// (include/core/page_attention.h:15). Explicit instantiation of a template
+// on a member pointer is exempt from access checking, which lets this file
+// read it without touching the reference's header; a public
+// `int32_t capacity() const` on BlockPool would replace these lines.
+struct CapacityTag {
+    using type = int32_t BlockPool::*;
+    friend type member(CapacityTag);
+};
+template <typename Tag, typename Tag::type M>
+struct Expose {
+    friend typename Tag::type member(Tag) { return M; }
+};
+template struct Expose<CapacityTag, &BlockPool::block_capacity_>;
+
+int32_t capacity(const BlockPool& p) { return p.*member(CapacityTag{}); }
+
+// Pages BlockPool::alloc can still hand out: its free list, then fresh ids
+// up to the capacity (src/core/page_attention.cpp:38-47).
+int32_t available(const BlockPool& p) { return p.num_free() + (capacity(p) - p.num_blocks()); }
+
+// New pages append_kv_pages takes for `count` tokens after `cached`: one per
+// position that starts a page (src/core/page_attention.cpp:146-157).
+int32_t pages_needed(int32_t cached, int32_t count) {
+    const int32_t first = (cached + PAGE_BLOCK_SIZE - 1) / PAGE_BLOCK_SIZE;
+    const int32_t last = (cached + count + PAGE_BLOCK_SIZE - 1) / PAGE_BLOCK_SIZE;
+    return last - first;
+}
 
 int32_t to_gkv_dtype(DataType d) {
     switch (d) {
@@ -82,13 +112,26 @@ void PagedAttentionImpl<Device::CUDA>::execute(Tensor* out, int32_t dev_id) {
     auto& layer = mgr->get_layer(layer_id);
     const int32_t prev_cached = layer.num_cached;
 
-    // Host allocation by the reference's own allocator.
+    // Host allocation by the reference's own allocator, checked first: if
+    // either pool cannot supply every page the chunk opens, nothing is
+    // allocated and the cache is left as it was.
+    const int32_t need = pages_needed(prev_cached, seq_len);
+    if (available(layer.k_pool) < need || available(layer.v_pool) < need)
+        throw std::runtime_error("paged_attention: KV page pool exhausted");
+    const size_t prev_pages = layer.page_table.size();
     mgr->append_kv_pages(layer_id, seq_len);
     const int32_t n_pages = static_cast<int32_t>(layer.page_table.size());
-    if (n_pages < (layer.num_cached + PAGE_BLOCK_SIZE - 1) / PAGE_BLOCK_SIZE) {
+    // On a failed launch the step is undone: num_cached restored, the pages
+    // it opened returned to the free lists, newest first, so the LIFO order
+    // of the next allocations is what it would have been.
+    auto undo = [&] {
         layer.num_cached = prev_cached;
-        throw std::runtime_error("paged_attention: KV page pool exhausted");
-    }
+        while (layer.page_table.size() > prev_pages) {
+            layer.k_pool.free(layer.page_table.back().k_block_id);
+            layer.v_pool.free(layer.page_table.back().v_block_id);
+            layer.page_table.pop_back();
+        }
+    };
 
     std::lock_guard<std::mutex> lock(g_mu);
     DeviceMirror& dm = g_mirrors[{mgr, layer_id}];
@@ -96,7 +139,10 @@ void PagedAttentionImpl<Device::CUDA>::execute(Tensor* out, int32_t dev_id) {
     if (!dm.table || dm.capacity < n_pages) {
         const int32_t cap = std::max<int32_t>(256, 2 * n_pages);
         gkv_table* t = nullptr;
-        if (gkv_table_create(dev_id, cap, &t) != GKV_OK) raise("device table");
+        if (gkv_table_create(dev_id, cap, &t) != GKV_OK) {
+            undo();
+            raise("device table");
+        }
         if (dm.table) gkv_table_destroy(dm.table);
         dm.table = t;
         dm.capacity = cap;
@@ -108,13 +154,15 @@ void PagedAttentionImpl<Device::CUDA>::execute(Tensor* out, int32_t dev_id) {
         v_ids.push_back(layer.page_table[i].v_block_id);
     }
     gkv_new_pages np{dm.published, static_cast<int32_t>(k_ids.size()), k_ids.data(), v_ids.data()};
+    // The pools' full reserved extent (fixed per layer, so the library's
+    // tensor maps are encoded once), not the allocation high-water mark.
     gkv_pool_desc pool{layer.k_pool.block_data(0), layer.v_pool.block_data(0),
-                       std::max(layer.k_pool.num_blocks(), layer.v_pool.num_blocks()), n_kv_heads, head_dim,
+                       std::min(capacity(layer.k_pool), capacity(layer.v_pool)), n_kv_heads, head_dim,
                        to_gkv_dtype(K->dtype)};
     if (gkv_paged_attention_raw(&pool, dm.table, prev_cached, &np, Q->data, K->data, V->data, out->data,
                                 n_q_heads, seq_len, scale, causal ? 1 : 0, to_gkv_dtype(out->dtype),
                                 nullptr) != GKV_OK) {
-        layer.num_cached = prev_cached;
+        undo();
         raise("launch");
     }
     dm.published = n_pages;

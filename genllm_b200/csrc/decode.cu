@@ -31,6 +31,7 @@
 // every mbarrier wait is bounded (kErrTimeout).
 #include <cstdlib>
 
+#include <algorithm>
 #include <atomic>
 
 #include "device.cuh"
@@ -40,8 +41,10 @@
 namespace gkv {
 namespace {
 
+// A stage holds kConsumerWarps (page, head) tiles of K and of V, one per
+// consumer warp; a producer warp keeps the ring of stages filled.
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + producer warp
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
 #ifdef GKV_PROBE_STAGES
 constexpr int kStages = GKV_PROBE_STAGES;
 #else
@@ -52,11 +55,11 @@ constexpr uint32_t kTile = 2 * kTileHalf;            // one (page, head) K or V 
 constexpr uint32_t kStageKV = kConsumerWarps * kTile;  // 32 KiB of K (or V) per stage
 constexpr uint32_t kStageBytes = 2 * kStageKV;        // 64 KiB
 constexpr uint32_t kOffBar = kStages * kStageBytes;
-constexpr uint32_t kOffP = kOffBar + 2 * kStages * 8;            // per-warp P^T hi/lo buffers
+constexpr uint32_t kOffP = kOffBar + 2 * kStages * 8;            // full barriers, slot counters; then per-warp P^T hi/lo buffers
 constexpr int kMaxSplitPages = 1024;                              // page ids cached per CTA
 constexpr uint32_t kOffIds = kOffP + kConsumerWarps * 512;
 constexpr uint32_t kSmemBytes = kOffIds + kMaxSplitPages * 8 + 1024;  // + alignment slack
-static_assert(kConsumerWarps * 8 * (kHeadDim + 2) * 4 <= kStages * kStageBytes, "merge buffers fit");
+static_assert(kConsumerWarps * 36 * 32 * 4 <= kStages * kStageBytes, "merge buffers fit");
 
 struct DecodeParams {
     const uint16_t* q;
@@ -68,6 +71,18 @@ struct DecodeParams {
     float* part_acc;   // [n_splits][Hq][128]
     float2* part_ml;   // [n_splits][Hq]
     uint32_t* err;
+    const uint32_t* done;  // non-null: wait until *done reaches done_expect before reading the table or pages
+    uint32_t done_expect;
+    // Split merge fused into this grid (null: the combine kernel merges).
+    // merge[0] counts arriving CTAs, merge[1] finished mergers; both zero
+    // between launches. The last n_merge CTAs to arrive merge the splits.
+    uint32_t* merge;
+    void* out;
+    int32_t out_dtype;
+    uint32_t* done_post;  // non-null (with merge): the last merger stores done_seq here
+    uint32_t done_seq;
+    int32_t late_trigger;  // 1: release the next launch only after this grid's wait for its predecessor
+    int32_t l2_prefetch_stages;  // stages past the ring brought into L2 while the ring is full
     int32_t n_kv_heads;
     int32_t group;     // G = Hq / Hkv
     int32_t pool_pages;
@@ -118,9 +133,31 @@ __device__ __forceinline__ bool entry_ok(const DecodeParams& a, int2 e) {
 }
 
 // Byte offset of (slot row r, 16-byte chunk c of the 128 dims) inside a
-// (page, head) tile stored as two 128-byte-swizzled 64-dim halves.
-__device__ __forceinline__ uint32_t tile_off(int r, int c) {
-    return (uint32_t)((c >> 3) * kTileHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+// (page, head) tile stored as two 128-byte-swizzled 64-dim halves of
+// 16 rows x 128 B, `hs` bytes apart (kTileHalf when a tile is contiguous,
+// Hkv * kTileHalf when a page's heads are interleaved half by half).
+__device__ __forceinline__ uint32_t tile_off(int r, int c, uint32_t hs) {
+    return (uint32_t)((c >> 3) * hs + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Wait (bounded) until the completion word of the table reaches `expect`:
+// every earlier decode step of this table has completed, so its appended
+// rows and published table entries can be read. Acquire at GPU scope, then
+// a proxy fence so that the TMA (async proxy) reads come after it.
+__device__ __forceinline__ void wait_done(const uint32_t* done, uint32_t expect, uint32_t* err) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
+    if ((int32_t)(v - expect) < 0) {
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t i = 0;; ++i) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
+            if ((int32_t)(v - expect) >= 0) break;
+            if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(err, kErrTimeout);
+                break;
+            }
+        }
+    }
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -144,15 +181,109 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+
+// One merge unit of the fused split merge: query head h, 64-dim half hf.
+// 18 groups of 16 threads; group gi folds splits gi, gi + 18, ... with an
+// online rescale (each thread 4 dims, float4 loads from L2: the partials are
+// this grid's own stores), then group 0 folds the 18 group results from
+// shared memory and stores the output.
+constexpr int kMergeGroups = kThreads / 16;  // 18
+constexpr int kMergeBatch = 9;               // splits per group in flight at once
+static_assert(kMergeGroups * 68 * 4 <= kStages * kStageBytes, "merge buffers fit");
+
+__device__ __noinline__ void merge_unit(const float* part_acc, const float2* part_ml, void* out, int out_dtype,
+                                       float* sbuf, int n_splits, int Hq, int h, int hf) {
+    const int gi = threadIdx.x >> 4, li = threadIdx.x & 15;
+    const int d = hf * 64 + li * 4;
+    float M = -INFINITY, L = 0.f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int b = 0; b * kMergeBatch * kMergeGroups < n_splits; ++b) {
+        float2 ml[kMergeBatch];
+        float4 av[kMergeBatch];
+#pragma unroll
+        for (int i = 0; i < kMergeBatch; ++i) {
+            const int sp = gi + (b * kMergeBatch + i) * kMergeGroups;
+            const bool in = sp < n_splits;
+            const size_t row = (size_t)sp * Hq + h;
+            ml[i] = in ? __ldcg(part_ml + row) : make_float2(-INFINITY, 0.f);
+            av[i] = in ? __ldcg(reinterpret_cast<const float4*>(part_acc + row * kHeadDim + d))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float mb = M;
+#pragma unroll
+        for (int i = 0; i < kMergeBatch; ++i) mb = fmaxf(mb, ml[i].x);
+        const float ms = mb == -INFINITY ? 0.f : mb;
+        const float r = exp2_approx(M - ms);
+        L *= r;
+        A.x *= r; A.y *= r; A.z *= r; A.w *= r;
+#pragma unroll
+        for (int i = 0; i < kMergeBatch; ++i) {
+            const float f = exp2_approx(ml[i].x - ms);
+            L = fmaf(ml[i].y, f, L);
+            A.x = fmaf(av[i].x, f, A.x);
+            A.y = fmaf(av[i].y, f, A.y);
+            A.z = fmaf(av[i].z, f, A.z);
+            A.w = fmaf(av[i].w, f, A.w);
+        }
+        M = mb;
+        if ((li & 7) == 0) {  // two 128-byte lines per (split, head, half), read by this group alone
+#pragma unroll
+            for (int i = 0; i < kMergeBatch; ++i) {
+                const int sp = gi + (b * kMergeBatch + i) * kMergeGroups;
+                if (sp < n_splits) l2_discard_line(part_acc + ((size_t)sp * Hq + h) * kHeadDim + d);
+            }
+        }
+    }
+    // sbuf: [group][m, l, 2 spare, 64 dims] (68 floats: 16-byte aligned rows)
+    float* mine = sbuf + gi * 68;
+    if (li == 0) {
+        mine[0] = M;
+        mine[1] = L;
+    }
+    *reinterpret_cast<float4*>(mine + 4 + li * 4) = A;
+    __syncthreads();
+    if (gi == 0) {
+        float Mt = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kMergeGroups; ++k) Mt = fmaxf(Mt, sbuf[k * 68]);
+        const float ms = Mt == -INFINITY ? 0.f : Mt;
+        float Lt = 0.f;
+        float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < kMergeGroups; ++k) {
+            const float* o = sbuf + k * 68;
+            const float f = exp2_approx(o[0] - ms);
+            const float4 v = *reinterpret_cast<const float4*>(o + 4 + li * 4);
+            Lt = fmaf(o[1], f, Lt);
+            At.x = fmaf(v.x, f, At.x);
+            At.y = fmaf(v.y, f, At.y);
+            At.z = fmaf(v.z, f, At.z);
+            At.w = fmaf(v.w, f, At.w);
+        }
+        const size_t base = (size_t)h * kHeadDim + d;
+        store_out(out, base + 0, At.x / Lt, out_dtype);
+        store_out(out, base + 1, At.y / Lt, out_dtype);
+        store_out(out, base + 2, At.z / Lt, out_dtype);
+        store_out(out, base + 3, At.w / Lt, out_dtype);
+    }
+    __syncthreads();
+}
+
 #ifdef GKV_PROBE_TIMELINE
 __device__ unsigned long long g_probe_tl[8 * 4096 * 8];
+__device__ unsigned long long g_probe_st[8 * 2048 * 16];  // stage-ready times seen by consumer warp 0
 #define PROBE_T(k) \
     if (threadIdx.x == 0) g_probe_tl[(a.probe_slot * 4096 + blockIdx.x) * 8 + (k)] = global_timer_ns();
 #else
 #define PROBE_T(k)
 #endif
 
-__global__ void __launch_bounds__(kThreads, 2)
+// kPageBox: one TMA box {64 dims, 16 slots, Hkv heads} per page and 64-dim
+// half (4 copies per page; the stage holds a page as [half][head][slot]);
+// otherwise one box {64 dims, 1 head, 16 slots} per (page, head, half) (32
+// copies per page at Hkv = 8; the stage holds [head][half][slot]).
+template <bool kPageBox>
+__global__ void __launch_bounds__(kThreads, 2)  // 96 registers: a combine CTA fits beside it
     paged_decode_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
                         const DecodeParams a) {
     extern __shared__ uint8_t smem_raw[];
@@ -172,14 +303,23 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int p1 = min(sf.n_pages, p0 + sf.pages_per_split);
     const int n_stages = p1 > p0 ? (p1 - p0 + P - 1) / P : 0;
 
+    // Programmatic dependent launch: the split-combine kernel that follows may
+    // be scheduled now (it waits for this grid's completion itself).
+    if (!a.late_trigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    // This grid may start before the previous decode step of the same table
+    // has completed (the combine kernels release their successor at entry):
+    // its table entries and appended rows are read only once its completion
+    // word says so.
+    if (a.done != nullptr) {
+        if (threadIdx.x == 0) wait_done(a.done, a.done_expect, a.err);
+        __syncthreads();
+    }
+
     // Publish this step's new block-table entries (this launch reads them
     // from its parameters; later launches read the table).
     if (split == 0 && (int)threadIdx.x < sf.new_n)
         a.table[sf.new_first + threadIdx.x] = threadIdx.x == 0 ? sf.new0 : a.new_ids[threadIdx.x];
-
-    // Programmatic dependent launch: the split-combine kernel that follows may
-    // be scheduled now (it waits for this grid's completion itself).
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // Stage i of this split: its np pages, every kv head, both 64-dim halves of
     // K and V, one TMA box {64, 1, 16} each, completing on full[i % kStages].
@@ -194,12 +334,41 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int pi = 0; pi < np; ++pi) {
             int2 e = entry_of(i * P + pi);
             if (e.x < 0) e = make_int2(0, 0);  // loaded but never used (the consumer skips it)
-            for (int h = 0; h < Hkv; ++h) {
-                const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
+            if constexpr (kPageBox) {
+                const uint32_t t = (uint32_t)(pi * Hkv) * kTile;
                 for (int hf = 0; hf < 2; ++hf) {
-                    tma_load_3d(sk + t + hf * kTileHalf, &k_map, &full[st], hf * 64, h, e.x * kPageSlots, pol);
-                    tma_load_3d(sv + t + hf * kTileHalf, &v_map, &full[st], hf * 64, h, e.y * kPageSlots, pol);
+                    const uint32_t o = t + (uint32_t)(hf * Hkv) * kTileHalf;
+                    tma_load_3d(sk + o, &k_map, &full[st], hf * 64, e.x * kPageSlots, 0, pol);
+                    tma_load_3d(sv + o, &v_map, &full[st], hf * 64, e.y * kPageSlots, 0, pol);
                 }
+            } else {
+                for (int h = 0; h < Hkv; ++h) {
+                    const uint32_t t = (uint32_t)(pi * Hkv + h) * kTile;
+                    for (int hf = 0; hf < 2; ++hf) {
+                        tma_load_3d(sk + t + hf * kTileHalf, &k_map, &full[st], hf * 64, h, e.x * kPageSlots, pol);
+                        tma_load_3d(sv + t + hf * kTileHalf, &v_map, &full[st], hf * 64, h, e.y * kPageSlots, pol);
+                    }
+                }
+            }
+        }
+    };
+    // Stage i's pages into L2 (no shared memory, no barrier).
+    auto prefetch_stage = [&](int i, auto&& entry_of) {
+        const int np = min(P, p1 - (p0 + i * P));
+        for (int pi = 0; pi < np; ++pi) {
+            const int2 e = entry_of(i * P + pi);
+            if (e.x < 0) continue;
+            if constexpr (kPageBox) {
+                for (int hf = 0; hf < 2; ++hf) {
+                    tma_prefetch_3d(&k_map, hf * 64, e.x * kPageSlots, 0);
+                    tma_prefetch_3d(&v_map, hf * 64, e.y * kPageSlots, 0);
+                }
+            } else {
+                for (int h = 0; h < Hkv; ++h)
+                    for (int hf = 0; hf < 2; ++hf) {
+                        tma_prefetch_3d(&k_map, hf * 64, h, e.x * kPageSlots);
+                        tma_prefetch_3d(&v_map, hf * 64, h, e.y * kPageSlots);
+                    }
             }
         }
     };
@@ -224,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_init(&empty[s], kConsumerWarps);
         }
         fence_mbar_init();
+        if (a.done != nullptr) asm volatile("fence.proxy.async.global;" ::: "memory");
         if (n_stages > 0) issue_stage(0, checked);
     }
     for (int i = threadIdx.x; i < p1 - p0; i += kThreads) ids[i] = checked(i);
@@ -238,12 +408,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (i >= kStages && !mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1))
                     atomicOr(a.err, kErrTimeout);
                 issue_stage(i, [&](int k) { return ids[k]; });
+                if (i == kStages - 1) {
+                    // The ring is full. Until the consumers may start (their
+                    // griddepcontrol.wait, which on the per-layer path waits
+                    // for the previous kernels to complete) nothing frees
+                    // it: bring the next stages' pages into L2 meanwhile, so
+                    // that their loads later come from L2 rather than HBM.
+                    const int pf_end = min(n_stages, kStages + a.l2_prefetch_stages);
+                    for (int j = kStages; j < pf_end; ++j) prefetch_stage(j, [&](int k) { return ids[k]; });
+                }
             }
         }
     } else {
         // ---------------- consumers ----------------
         const int head = warp % Hkv;
         const int pslot = warp / Hkv;           // page within a stage
+        const uint32_t hs = kPageBox ? (uint32_t)Hkv * kTileHalf : kTileHalf;  // 64-dim halves apart
         const bool active = pslot < P;
         const int g = lane >> 2;                // fragment row group
         const int t = lane & 3;                 // fragment column pair
@@ -265,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // first launch: no wait here (one thread waits at the end instead, so
         // that this grid still completes after the previous kernel).
         if (!a.inputs_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (a.late_trigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         PROBE_T(5);
         // B operand of S^T = K Q^T: Q^T fragments (k = dims, n = grouped query head).
         uint32_t qb[8][2];
@@ -345,6 +526,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int st = i % kStages;
             const bool ok_wait = mbar_wait_bounded(&full[st], (i / kStages) & 1);
             if (i == 0) { PROBE_T(2); }
+#ifdef GKV_PROBE_TIMELINE
+            if (threadIdx.x == 0 && i < 16) g_probe_st[(a.probe_slot * 2048 + blockIdx.x) * 16 + i] = global_timer_ns();
+#endif
             if (!ok_wait && lane == 0) atomicOr(a.err, kErrTimeout);
             const int lp = p0 + i * P + pslot;
             const bool have = active && lp < p1 && ok_wait;
@@ -356,7 +540,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             const bool use = have && e.x >= 0;
 #endif
             if (use) {
-                uint8_t* kt = smem + st * kStageBytes + (uint32_t)(pslot * Hkv + head) * kTile;
+                uint8_t* kt = smem + st * kStageBytes +
+                              (kPageBox ? (uint32_t)(pslot * Hkv) * kTile + (uint32_t)head * kTileHalf
+                                        : (uint32_t)(pslot * Hkv + head) * kTile);
                 uint8_t* vt = kt + kStageKV;
                 const int base = lp * kPageSlots;
                 const int nvalid = min(kPageSlots, sf.total - base);
@@ -381,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                         kk = *reinterpret_cast<const uint2*>(a.k_new + (size_t)head * kHeadDim + lane * 4);
                     }
                     const uint2 vv = *reinterpret_cast<const uint2*>(a.v_new + (size_t)head * kHeadDim + lane * 4);
-                    const uint32_t o = tile_off(slot, lane >> 1) + (lane & 1) * 8;
+                    const uint32_t o = tile_off(slot, lane >> 1, hs) + (lane & 1) * 8;
                     *reinterpret_cast<uint2*>(kt + o) = kk;
                     *reinterpret_cast<uint2*>(vt + o) = vv;
                     const size_t row = ((size_t)slot * Hkv + head) * kHeadDim + lane * 4;
@@ -392,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (nvalid < kPageSlots) {
                     for (int r = nvalid + (lane >> 3); r < kPageSlots; r += 4) {
                         *reinterpret_cast<uint4*>(vt + r * 128 + (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
-                        *reinterpret_cast<uint4*>(vt + kTileHalf + r * 128 + (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(vt + hs + r * 128 + (lane & 7) * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
                 __syncwarp();
@@ -404,8 +590,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                 for (int kk = 0; kk < 8; kk += 2) {
                     uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-                    ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
-                    ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + 2 + (mi >> 1)), b0, b1, b2, b3);
+                    ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + (mi >> 1), hs), a0, a1, a2, a3);
+                    ldsm_x4(ks + tile_off(lr + (mi & 1) * 8, 2 * kk + 2 + (mi >> 1), hs), b0, b1, b2, b3);
                     mma_bf16_16816(s, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
                     mma_bf16_16816(s_odd, b0, b1, b2, b3, qb[kk + 1][0], qb[kk + 1][1]);
                 }
@@ -468,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                 for (int mt = 0; mt < 8; ++mt) {
                     uint32_t a0, a1, a2, a3;
-                    ldsm_x4_t(vs + tile_off(lr + (mi >> 1) * 8, 2 * mt + (mi & 1)), a0, a1, a2, a3);
+                    ldsm_x4_t(vs + tile_off(lr + (mi >> 1) * 8, 2 * mt + (mi & 1), hs), a0, a1, a2, a3);
                     mma_bf16_16816(acc[mt], a0, a1, a2, a3, ph0, ph1);
                     mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
                 }
@@ -478,9 +664,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
-        // Warps that share a kv head (P > 1) merge in registers through shared
-        // memory, in fragment order (lane-major, conflict-free); then the warp
-        // of page slot 0 holds the CTA's partial for its head.
+        // Warps that share a kv head (P > 1 pages per stage) merge in
+        // registers through shared memory, in fragment order (lane-major,
+        // conflict-free); then the warp of page slot 0 holds the CTA's
+        // partial for its head.
         if (P > 1) {
             asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));  // stage buffers are free
             float* frag = reinterpret_cast<float*>(smem);                 // [warp][36][32]
@@ -494,10 +681,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             mine[34 * 32] = m1;
             mine[35 * 32] = l1;
             asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+            auto peer = [&](int k) { return frag + (k * Hkv + head) * 36 * 32 + lane; };
             if (active && pslot == 0) {
                 float M0 = m0, M1 = m1;
-                for (int ps = 1; ps < P; ++ps) {
-                    const float* o = frag + (ps * Hkv + head) * 36 * 32 + lane;
+                for (int k = 1; k < P; ++k) {
+                    const float* o = peer(k);
                     M0 = fmaxf(M0, o[32 * 32]);
                     M1 = fmaxf(M1, o[34 * 32]);
                 }
@@ -512,8 +700,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                     acc[mt][2] *= f0;
                     acc[mt][3] *= f1;
                 }
-                for (int ps = 1; ps < P; ++ps) {
-                    const float* o = frag + (ps * Hkv + head) * 36 * 32 + lane;
+                for (int k = 1; k < P; ++k) {
+                    const float* o = peer(k);
                     const float g0 = exp2_approx(o[32 * 32] - s0), g1 = exp2_approx(o[34 * 32] - s1);
                     l0 = fmaf(o[33 * 32], g0, l0);
                     l1 = fmaf(o[35 * 32], g1, l1);
@@ -538,18 +726,75 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (n < G) {
                     const size_t row = (size_t)split * Hq + head * G + n;
                     float* dst = a.part_acc + row * kHeadDim;
+                    // Kept in L2 (evict_last) until the merge reads them: the
+                    // next decode grid streams pages into L2 meanwhile.
+                    const uint64_t keep = l2_policy_evict_last();
 #pragma unroll
                     for (int mt = 0; mt < 8; ++mt) {
-                        dst[mt * 16 + g] = acc[mt][half];
-                        dst[mt * 16 + g + 8] = acc[mt][2 + half];
+                        st_f32_hint(dst + mt * 16 + g, acc[mt][half], keep);
+                        st_f32_hint(dst + mt * 16 + g + 8, acc[mt][2 + half], keep);
                     }
-                    if (g == 0) a.part_ml[row] = half ? make_float2(m1, l1) : make_float2(m0, l0);
+                    if (g == 0) {
+                        const float2 ml = half ? make_float2(m1, l1) : make_float2(m0, l0);
+                        st_f32_hint(&a.part_ml[row].x, ml.x, keep);
+                        st_f32_hint(&a.part_ml[row].y, ml.y, keep);
+                    }
                 }
             }
         }
     }
-    __syncthreads();
-    PROBE_T(3);
+    if (a.merge != nullptr) {
+        // ---------------- fused split merge ----------------
+        // This CTA's partials (and the appended row / table entries) are
+        // ordered before its arrival; the last n_merge CTAs to arrive wait
+        // (bounded) for the others, then merge one or more (head, half) units.
+        // Splits past the step's count (a captured step's fixed grid) had no
+        // pages and take no part.
+        const int n_splits = a.step ? __ldg(&a.step->n_splits) : (int)gridDim.x;
+        const int n_merge = min(n_splits, 2 * Hkv * G);
+        __threadfence();
+        __syncthreads();
+        __shared__ uint32_t s_ticket;
+        if (threadIdx.x == 0 && split < n_splits) s_ticket = atomicAdd(&a.merge[0], 1u);
+        __syncthreads();
+        PROBE_T(3);
+        const uint32_t first = (uint32_t)(n_splits - n_merge);
+        if (split < n_splits && s_ticket >= first) {
+            if (threadIdx.x == 0) {
+                uint32_t v;
+                const uint64_t t0 = global_timer_ns();
+                for (uint32_t i = 0;; ++i) {
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.merge) : "memory");
+                    if (v >= (uint32_t)n_splits) break;
+                    if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                        atomicOr(a.err, kErrTimeout);
+                        break;
+                    }
+                }
+            }
+            __syncthreads();
+            PROBE_T(7);
+            const int Hq = Hkv * G;
+            float* sbuf = reinterpret_cast<float*>(smem);  // stage buffers are free
+            for (int u = (int)(s_ticket - first); u < 2 * Hq; u += n_merge) merge_unit(a.part_acc, a.part_ml, a.out, a.out_dtype, sbuf, n_splits, Hq, u >> 1, u & 1);
+            if (threadIdx.x == 0) {
+                __threadfence();
+                if (atomicAdd(&a.merge[1], 1u) == (uint32_t)n_merge - 1u) {
+                    // Every merger has read the partials: reset for the next
+                    // launch, and publish this step's completion for the next
+                    // decode step of the table.
+                    a.merge[0] = 0u;
+                    a.merge[1] = 0u;
+                    if (a.done_post != nullptr)
+                        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.done_post), "r"(a.done_seq)
+                                     : "memory");
+                }
+            }
+        }
+    } else {
+        __syncthreads();
+        PROBE_T(3);
+    }
     if (a.inputs_ready && threadIdx.x == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 
 #ifdef GKV_PROBE_TIMELINE
@@ -569,6 +814,8 @@ struct CombineParams {
     GatherLaunch g;
     const DeviceStep* step;  // non-null: n_splits from here (captured steps)
     int32_t early;           // 1: the next launch is another layer's decode: trigger it at entry
+    uint32_t* done;          // non-null: post done_seq here once the decode grid completed; trigger at entry
+    uint32_t done_seq;
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
 #endif
@@ -591,16 +838,26 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     // whose layers are distinct, and not its last layer), it reads nothing
     // this layer's grids write before its own wait: it may start now, its
     // page stream overlapping this layer's tail.
+    // With a completion word, a decode launched next reads nothing before its
+    // own wait that this step wrote until the word says this step completed
+    // (it checks it), so it may start now whatever layer it belongs to: its
+    // page stream overlaps this step's tail, this merge and (multi-GPU) the
+    // gather's completion protocol.
     const bool gather = c.g.world > 1;
-    if (c.early && !gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const bool early = c.done != nullptr || (c.early && !gather);
+    if (early) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
     PROBE_C(1);
+    // The decode grid has completed: its pool rows and table entries are
+    // visible. Publish that for the next decode step of this table.
+    if (c.done != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(c.done), "r"(c.done_seq) : "memory");
     // Otherwise only now may the next launch start: a decode step of the
     // same layer reads pages and table entries this step's decode grid
     // wrote, and its page stream begins before it waits for this grid. With
     // the fused gather the trigger comes after this rank's stores and flags
     // are out.
-    if (!c.early && !gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!early && !gather) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int hq = blockIdx.x;
     const int lane = threadIdx.x & 31;
     const int d = blockIdx.y * kCombineDims + lane;
@@ -634,6 +891,15 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
             A = fmaf(av[i], f, A);
         }
         M = mb;
+        // Each 128-byte line of partials (one split, 32 dims) is read by this
+        // warp alone: drop it from L2 without a write-back.
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+                const int s = w + (b * kBatch + i) * kCombineWarps;
+                if (s < n_splits) l2_discard_line(c.part_acc + ((size_t)s * c.n_q_heads + hq) * kHeadDim + blockIdx.y * kCombineDims);
+            }
+        }
     }
     if (lane == 0) {
         s_m[w] = M;
@@ -698,7 +964,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
         for (uint32_t i = 0;; ++i) {
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
             if ((int32_t)(v - c.g.epoch) >= 0) break;
-            if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+            if ((i & 63u) == 63u && global_timer_ns() - t0 > c.g.wait_ns) {
                 atomicOr(c.err, kErrTimeout);
                 break;
             }
@@ -715,6 +981,28 @@ bool overlap_enabled() {
     return on;
 }
 
+// Stages past the shared-memory ring that the producer brings into L2
+// while the ring is full (GKV_DECODE_L2_PREFETCH, default 0: measured at 32k,
+// the prefetch traffic slows the previous layer's merge by more than the
+// early pages save on per-layer calls).
+int l2_prefetch_stages() {
+    static const int n = [] {
+        const char* v = getenv("GKV_DECODE_L2_PREFETCH");
+        return v ? atoi(v) : 0;
+    }();
+    return n;
+}
+
+// GKV_DECODE_BOX=head selects the per-(page, head) boxes; the default is one
+// box per page and 64-dim half.
+bool page_boxes() {
+    static const bool on = [] {
+        const char* v = getenv("GKV_DECODE_BOX");
+        return !(v && v[0] == 'h');
+    }();
+    return on;
+}
+
 }  // namespace
 
 cudaError_t configure_decode_kernels() {
@@ -723,13 +1011,15 @@ cudaError_t configure_decode_kernels() {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 64 || !(configured.load() & (1ull << dev))) {
-        e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-        if (e != cudaSuccess) return e;
         // Both kernels ask for the largest shared-memory carveout, so that an
         // SM running combine CTAs can take the next decode CTA without
         // reconfiguring (which would wait for the combine CTAs to drain).
-        e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        if (e != cudaSuccess) return e;
+        for (auto* k : {paged_decode_kernel<false>, paged_decode_kernel<true>}) {
+            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+            if (e != cudaSuccess) return e;
+            e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            if (e != cudaSuccess) return e;
+        }
         e = cudaFuncSetAttribute(paged_decode_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured.fetch_or(1ull << dev);
@@ -756,7 +1046,7 @@ bool decode_split_geometry(int32_t n_pages, int32_t n_kv_heads, int32_t n_q_head
     return true;
 }
 
-cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map, int2* table,
+cudaError_t launch_decode(const PoolView& pool, const DecodeMaps& maps, int2* table,
                           const NewPages& np, const Scratch& scratch, const DecodeLaunch& d, int num_sms,
                           cudaStream_t stream, const GatherLaunch* gather) {
     const int Hkv = pool.n_kv_heads;
@@ -773,6 +1063,14 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     p.part_acc = scratch.part_acc;
     p.part_ml = scratch.part_ml;
     p.err = scratch.err;
+    p.done = d.post_done ? scratch.done : nullptr;
+    p.done_expect = d.done_seq - 1u;
+    p.merge = nullptr;
+    p.out = d.out;
+    p.out_dtype = d.out_dtype;
+    p.done_post = nullptr;
+    p.done_seq = d.done_seq;
+    p.l2_prefetch_stages = l2_prefetch_stages();
     p.n_kv_heads = Hkv;
     p.group = d.n_q_heads / Hkv;
     p.pool_pages = pool.pool_pages;
@@ -798,6 +1096,19 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     p.step = d.step;
     p.inputs_ready = d.prev_is_other_layer ? 1 : 0;
     int grid = n_splits;
+    // The split merge runs inside the decode grid (no combine launch) with
+    // the table's own counters; the fused multi-GPU gather keeps the combine
+    // kernel.
+    const bool fused = d.fused_merge && scratch.merge != nullptr && !(gather && gather->world > 1);
+    p.late_trigger = 0;
+    if (fused) {
+        p.merge = scratch.merge;
+        p.done_post = d.post_done ? scratch.done : nullptr;
+        // The first layer of an uncaptured multi-layer step: the next layer's
+        // decode reads its inputs without waiting, so it may start only once
+        // this grid has waited for whatever ran before the step.
+        p.late_trigger = d.next_is_other_layer && !d.prev_is_other_layer && !d.step ? 1 : 0;
+    }
     if (d.step) {
         // Captured step: the geometry in the step block changes from token
         // to token; the grid is fixed and splits past the step's count find
@@ -820,13 +1131,18 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
     dcfg.stream = stream;
     dcfg.attrs = attr;
     dcfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&dcfg, paged_decode_kernel, k_map, v_map, p);
+    const bool pb = page_boxes();
+    e = pb ? cudaLaunchKernelEx(&dcfg, paged_decode_kernel<true>, maps.k_page, maps.v_page, p)
+           : cudaLaunchKernelEx(&dcfg, paged_decode_kernel<false>, maps.k_head, maps.v_head, p);
     if (e != cudaSuccess) return e;
+    if (fused) return cudaSuccess;
 
     CombineParams c{scratch.part_acc, scratch.part_ml, d.out, d.out_dtype, d.n_q_heads, n_splits, scratch.err, {}};
     if (gather) c.g = *gather;
     c.step = d.step;
     c.early = d.next_is_other_layer ? 1 : 0;
+    c.done = d.post_done ? scratch.done : nullptr;
+    c.done_seq = d.done_seq;
 #ifdef GKV_PROBE_TIMELINE
     c.probe_slot = p.probe_slot;
 #endif
@@ -845,5 +1161,8 @@ cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const 
 #ifdef GKV_PROBE_TIMELINE
 extern "C" int gkv_probe_read_timeline(unsigned long long* out, int n) {
     return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_tl, sizeof(unsigned long long) * n);
+}
+extern "C" int gkv_probe_read_stages(unsigned long long* out, int n) {
+    return (int)cudaMemcpyFromSymbol(out, gkv::g_probe_st, sizeof(unsigned long long) * n);
 }
 #endif

@@ -85,6 +85,24 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     return pol;
 }
 
+// L2 policy for data written now and read back soon by another CTA or
+// kernel (split partials) while other traffic streams through L2.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void st_f32_hint(float* p, float v, uint64_t policy) {
+    asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(policy) : "memory");
+}
+
+// Drop a 128-byte L2 line without writing it back (data read for the last
+// time, e.g. split partials once merged).
+__device__ __forceinline__ void l2_discard_line(const void* p) {
+    asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
 // 3-D tiled TMA load (no multicast) completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2, uint64_t policy) {
@@ -94,6 +112,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2),
         "l"(policy)
         : "memory");
+}
+
+// 3-D tiled TMA prefetch of a box into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
 }
 
 __device__ __forceinline__ float exp2_approx(float x) {

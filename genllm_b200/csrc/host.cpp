@@ -138,6 +138,17 @@ bool encode_pool_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMa
            encode(v_map, pool.v_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
 }
 
+bool encode_decode_maps(const PoolView& pool, DecodeMaps* m, const char** why) {
+    if (!encode_pool_maps_sw128(pool, &m->k_head, &m->v_head, why)) return false;
+    // [slots][heads][128] viewed as (dims, slots, heads): a box {64, 16, Hkv}
+    // lands in shared memory as [head][slot][64 dims].
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)pool.pool_pages * kPageSlots, (cuuint64_t)pool.n_kv_heads};
+    cuuint64_t strides[2] = {(cuuint64_t)pool.n_kv_heads * kHeadDim * 2, (cuuint64_t)kHeadDim * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)kPageSlots, (cuuint32_t)pool.n_kv_heads};
+    return encode(&m->k_page, pool.k_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why) &&
+           encode(&m->v_page, pool.v_base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, why);
+}
+
 bool encode_pool_run_maps_sw128(const PoolView& pool, CUtensorMap* k_map, CUtensorMap* v_map, const char** why) {
     cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)pool.n_kv_heads, (cuuint64_t)pool.pool_pages * 16};
     cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)pool.n_kv_heads * kHeadDim * 2};
@@ -179,6 +190,8 @@ struct gkv_table {
     int32_t map_pages = -1;
     int32_t map_heads = -1;
     CUtensorMap k_map_sw;   // box {64 dims, 1 head, 16 slots}, 128-byte swizzle
+    gkv::DecodeMaps dmaps;  // the decode kernel's maps of the same pool
+    uint32_t posted = 0;    // decode steps numbered so far (completion word protocol, kernels.h)
     CUtensorMap v_map_sw;
     CUtensorMap k_map_run;  // box {64 dims, 1 head, 128 slots}: 8 pages with consecutive ids
     CUtensorMap v_map_run;
@@ -230,7 +243,8 @@ int table_maps(gkv_table* t, const gkv_pool_desc* pool) {
     gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
                      pool->pool_pages, pool->n_kv_heads};
     const char* why = nullptr;
-    if (!gkv::encode_pool_maps_sw128(pv, &t->k_map_sw, &t->v_map_sw, &why))
+    if (!gkv::encode_pool_maps_sw128(pv, &t->k_map_sw, &t->v_map_sw, &why) ||
+        !gkv::encode_decode_maps(pv, &t->dmaps, &why))
         return fail(GKV_ERR_CUDA, "%s", why);
     t->runs = pool->pool_pages * 16 >= gkv::kRunSlots;
     if (t->runs && !gkv::encode_pool_run_maps_sw128(pv, &t->k_map_run, &t->v_map_run, &why))
@@ -352,16 +366,19 @@ int gkv_table_create(int device, int32_t capacity, gkv_table** out) {
     t->capacity = capacity;
     cudaDeviceGetAttribute(&t->num_sms, cudaDevAttrMultiProcessorCount, device);
     cudaError_t e;
+    t->scratch.err = nullptr;
     if ((e = cudaMalloc(&t->d_table, sizeof(int2) * (size_t)capacity)) != cudaSuccess ||
         (e = cudaMemset(t->d_table, 0xFF, sizeof(int2) * (size_t)capacity)) != cudaSuccess ||
         (e = cudaMalloc(&t->scratch.part_acc, sizeof(float) * gkv::kMaxPartialRows * 128)) != cudaSuccess ||
         (e = cudaMalloc(&t->scratch.part_ml, sizeof(float2) * gkv::kMaxPartialRows)) != cudaSuccess ||
-        (e = cudaMalloc(&t->scratch.err, sizeof(uint32_t))) != cudaSuccess ||
-        (e = cudaMemset(t->scratch.err, 0, sizeof(uint32_t))) != cudaSuccess) {
+        (e = cudaMalloc(&t->scratch.err, 256)) != cudaSuccess ||
+        (e = cudaMemset(t->scratch.err, 0, 256)) != cudaSuccess) {
         table_free(t);
         delete t;
         return cuda_fail(e, "gkv_table_create");
     }
+    t->scratch.done = t->scratch.err + 32;   // its own 128-byte line beside the error word
+    t->scratch.merge = t->scratch.err + 48;  // fused split merge counters
     *out = t;
     return GKV_OK;
 }
@@ -489,6 +506,18 @@ int check_qk(const gkv_qk_norm* qk, int32_t start, int32_t seq_len) {
     return GKV_OK;
 }
 
+// GKV_DECODE_FUSED_MERGE=1: the decode merges its splits inside its own
+// grid (the last CTAs to finish merge) instead of the combine kernel. Off by
+// default: measured at 32k it is level with the combine on per-layer calls
+// and slower inside a multi-layer step.
+bool fused_merge_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("GKV_DECODE_FUSED_MERGE");
+        return v && v[0] == '1';
+    }();
+    return on;
+}
+
 int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np, const void* Q,
                   const void* K, const void* V, void* out, int32_t n_q_heads, int32_t seq_len, float scale,
                   int32_t causal, int32_t out_dtype, const gkv::QkNorm* qk, gkv_stream_t stream) {
@@ -539,9 +568,15 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
         d.qk = qk;
         d.next_is_other_layer = t_next_other_layer;
         d.prev_is_other_layer = t_prev_other_layer;
-        cudaError_t e =
-            gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, p, t->scratch, d, t->num_sms, s, t_gather);
+        // A single step (not part of a multi-layer step) numbers itself on
+        // the table's completion word, so that its combine can release the
+        // next launch at entry.
+        d.post_done = !t_next_other_layer && !t_prev_other_layer;
+        d.done_seq = t->posted + 1u;
+        d.fused_merge = fused_merge_enabled();
+        cudaError_t e = gkv::launch_decode(pv, t->dmaps, t->d_table, p, t->scratch, d, t->num_sms, s, t_gather);
         if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+        if (d.post_done) t->posted = d.done_seq;
         return GKV_OK;
     }
 
@@ -1120,8 +1155,9 @@ int capture_decode_graph(gkv_decode_graph* g, int b, const void* const* Q, const
             // inputs are complete when layer 0's decode starts.
             d.next_is_other_layer = i + 1 < n;
             d.prev_is_other_layer = i > 0;
+            d.fused_merge = fused_merge_enabled();
             gkv::NewPages none{};
-            e = gkv::launch_decode(pv, t->k_map_sw, t->v_map_sw, t->d_table, none, t->scratch, d, t->num_sms, cs);
+            e = gkv::launch_decode(pv, t->dmaps, t->d_table, none, t->scratch, d, t->num_sms, cs);
         }
         cudaGraph_t graph = nullptr;
         const cudaError_t e2 = cudaStreamEndCapture(cs, &graph);
@@ -1497,6 +1533,7 @@ struct gkv_gather {
     uint32_t* flags[gkv::kMaxGatherRanks] = {};
     uint32_t* tickets = nullptr;  // [max_layers], zero between launches
     std::vector<uint32_t> epochs;  // calls so far per layer
+    uint64_t wait_ns = 1000ull * 1000ull * 1000ull;  // limit of the wait for the peers' flags (1 s)
 };
 
 extern "C" {
@@ -1571,6 +1608,13 @@ int gkv_gather_create(int device, int world, int rank, int max_layers, void* con
     return GKV_OK;
 }
 
+int gkv_gather_set_wait_limit(gkv_gather* gg, uint64_t limit_ns) {
+    if (!gg || limit_ns < 1000ull || limit_ns > 10ull * 1000 * 1000 * 1000)
+        return fail(GKV_ERR_INVALID, "gkv_gather_set_wait_limit: limit must be 1 us to 10 s");
+    gg->wait_ns = limit_ns;
+    return GKV_OK;
+}
+
 int gkv_gather_destroy(gkv_gather* gg) {
     if (!gg) return GKV_OK;
     DeviceGuard g(gg->device);
@@ -1601,6 +1645,7 @@ int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, 
     gl.flag_wait = gg->flags[gg->rank] + (size_t)layer_id * gg->world;
     gl.epoch = gg->epochs[layer_id] + 1;
     gl.ticket = gg->tickets + layer_id;
+    gl.wait_ns = gg->wait_ns;
     // The managed decode path, with this gather attached to its combine launch.
     t_gather = &gl;
     const int st = gkv_paged_attention(m, layer_id, Q, K, V, gl.dst[gg->rank], 1, n_q_heads, 1, 128, L->n_kv_heads,

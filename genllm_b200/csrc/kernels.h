@@ -27,6 +27,8 @@ struct Scratch {
     float* part_acc;     // [kMaxPartialRows][128] un-normalised split outputs
     float2* part_ml;     // [kMaxPartialRows] (running max in log2 units, sum)
     uint32_t* err;       // device error word
+    uint32_t* done = nullptr;  // completion word of the table's decode steps (see DecodeLaunch::post_done)
+    uint32_t* merge = nullptr; // two zeroed counters of the fused split merge (see DecodeLaunch::fused_merge)
 };
 
 struct PoolView {
@@ -83,6 +85,19 @@ struct DecodeLaunch {
     bool prev_is_other_layer = false;  // the previous launch is the combine of an earlier layer of the
                                        // same multi-layer step (launched with next_is_other_layer), and
                                        // Q / K / V were complete before the step's first launch
+    // Completion word protocol (scratch.done must be set): the decode grid
+    // waits until the word reaches done_seq - 1 (the table's previous decode
+    // step completed) before it reads the table or any page, and the combine
+    // stores done_seq once this step's decode grid has completed. The combine
+    // then releases the next launch at entry. The caller numbers the steps of
+    // a table 1, 2, 3, ... and only launches that post the word may be
+    // numbered.
+    bool post_done = false;
+    uint32_t done_seq = 0;
+    // Merge the splits inside the decode grid (the last CTAs to finish
+    // merge; scratch.merge must be set) instead of a combine launch. Not
+    // with a captured step or a multi-GPU gather.
+    bool fused_merge = false;
 };
 
 // Split geometry of a decode step: pages per split and the number of splits
@@ -109,12 +124,21 @@ struct GatherLaunch {
     const uint32_t* flag_wait;            // this layer's slots on this rank, world entries
     uint32_t epoch;                       // call count of this layer, 1-based
     uint32_t* ticket;                     // CTA completion counter (zero between launches)
+    uint64_t wait_ns;                     // limit of the wait for the peers' flags
 };
 
 // Fused decode step: append one token's K/V, GQA-grouped split-K
 // flash-decoding over the block table (k_map/v_map: the pool's 128-byte
 // swizzled maps), then the split combine. Returns the CUDA error.
-cudaError_t launch_decode(const PoolView& pool, const CUtensorMap& k_map, const CUtensorMap& v_map,
+// The decode kernel's tensor maps of a pool: per (page, head) boxes
+// {64, 1, 16} and per page boxes {64, 16 slots, Hkv heads}, 128-byte swizzle.
+struct DecodeMaps {
+    CUtensorMap k_head, v_head;
+    CUtensorMap k_page, v_page;
+};
+bool encode_decode_maps(const PoolView& pool, DecodeMaps* m, const char** why);
+
+cudaError_t launch_decode(const PoolView& pool, const DecodeMaps& maps,
                           int2* table, const NewPages& np, const Scratch& scratch,
                           const DecodeLaunch& d, int num_sms, cudaStream_t stream,
                           const GatherLaunch* gather = nullptr);

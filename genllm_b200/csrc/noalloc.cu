@@ -80,18 +80,21 @@ extern "C" int gkv_paged_decode_static_scratch(const gkv_pool_desc* pool, const 
         sms = g_sms[dev];
     }
     // Splits are capped so that the partial rows (splits x query heads) fit
-    // the static rows.
+    // the static rows; the geometry the launch will use (which may add
+    // splits for very long contexts) is checked against the same bound.
     int n_splits = sms;
     if (n_splits * n_q_heads > kStaticRows) n_splits = kStaticRows / n_q_heads;
     if (n_splits < 1) return fail(GKV_ERR_UNSUPPORTED, "too many query heads for the static scratch");
-    if ((long long)n_pages > 1000LL * n_splits)
+    int32_t pages_per_split = 0, used_splits = 0;
+    if (!decode_split_geometry(n_pages, pool->n_kv_heads, n_q_heads, n_splits, sms, &pages_per_split, &used_splits) ||
+        (long long)used_splits * n_q_heads > kStaticRows)
         return fail(GKV_ERR_INVALID, "context longer than the static scratch supports");
 
     PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base), pool->pool_pages,
                 pool->n_kv_heads};
-    CUtensorMap km, vm;
+    DecodeMaps maps;
     const char* why = nullptr;
-    if (!encode_pool_maps_sw128(pv, &km, &vm, &why)) return fail(GKV_ERR_CUDA, why);
+    if (!encode_decode_maps(pv, &maps, &why)) return fail(GKV_ERR_CUDA, why);
 
     Scratch sc;
     sc.part_acc = reinterpret_cast<float*>(base);
@@ -117,7 +120,31 @@ extern "C" int gkv_paged_decode_static_scratch(const gkv_pool_desc* pool, const 
     d.n_pages = n_pages;
     d.scale = scale;
     d.n_splits = n_splits;
-    e = launch_decode(pv, km, vm, reinterpret_cast<int2*>(const_cast<int32_t*>(device_table)), np, sc, d, sms, s);
+    e = launch_decode(pv, maps, reinterpret_cast<int2*>(const_cast<int32_t*>(device_table)), np, sc, d, sms, s);
     if (e != cudaSuccess) return fail(GKV_ERR_CUDA, cudaGetErrorString(e));
+    return GKV_OK;
+}
+
+extern "C" int gkv_paged_decode_static_scratch_errors(uint32_t* flags, gkv_stream_t stream) {
+    using namespace gkv;
+    if (!flags) return fail(GKV_ERR_INVALID, "null flags");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return fail(GKV_ERR_CUDA, "cannot query the current device");
+    unsigned char* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        base = g_addr[dev];
+    }
+    if (!base) {  // no decode call on this device yet
+        *flags = 0;
+        return GKV_OK;
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint32_t v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, base + kAccBytes + kMlBytes, sizeof(v), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(GKV_ERR_CUDA, cudaGetErrorString(e));
+    *flags = v;
     return GKV_OK;
 }

@@ -44,6 +44,7 @@ class DecodeWorkload:
     def __init__(self, device: int, n_layers=36, ctx=32768, pool_pages=4096, n_q_heads=32, n_kv_heads=8,
                  head_dim=128, seed=0, world=1, rank=0):
         self.device = torch.device("cuda", device)
+        self.seed = seed
         self.n_layers, self.ctx, self.pool_pages = n_layers, ctx, pool_pages
         self.Hq, self.Hkv, self.D = n_q_heads, n_kv_heads, head_dim
         qb, qe, kb, ke = shard_heads(n_q_heads, n_kv_heads, world, rank)
@@ -111,6 +112,41 @@ class DecodeWorkload:
         st = self._fn(*self._args[l], stream_handle)
         if st:
             _lib.check(st)
+
+    def reference_output(self, layer: int) -> torch.Tensor:
+        """Self-check of a bench run: the layer's attention output over every
+        cached token, all heads (not only this rank's), in plain torch fp32 on
+        the device, from the workload's seeded values regenerated in full:
+        the pool pages for the first ``ctx`` tokens, the step's K/V row (the
+        same every step) for the tokens appended since. Returns [Hq, D]."""
+        hkv, d, seed = self.Hkv, self.D, self.seed
+        g = torch.Generator(device=self.device)
+        pools = []
+        for off in (1, 2):
+            g.manual_seed(seed * 1000003 + layer * 7 + off)
+            chunks = [torch.randn((min(self.pool_pages, p0 + 512) - p0, PAGE, hkv, d), generator=g,
+                                  device=self.device).to(torch.bfloat16)
+                      for p0 in range(0, self.pool_pages, 512)]
+            pools.append(torch.cat(chunks))
+        g.manual_seed(seed * 1000003 + layer * 7 + 3)
+        q = torch.randn((self.Hq, d), generator=g, device=self.device).to(torch.bfloat16).float()
+        k_new = torch.randn((hkv, d), generator=g, device=self.device).to(torch.bfloat16).float()
+        v_new = torch.randn((hkv, d), generator=g, device=self.device).to(torch.bfloat16).float()
+        total = self.cached(layer)
+        table = self.mgr.get_layer(layer).page_table
+        ids = torch.tensor([[e.k_block_id, e.v_block_id] for e in table], dtype=torch.long, device=self.device)
+        pos = torch.arange(total, device=self.device)
+        rows = []
+        for w, new in ((0, k_new), (1, v_new)):
+            r = pools[w][ids[pos // PAGE, w], pos % PAGE].float()  # [total, Hkv, D]
+            r[self.ctx:] = new
+            rows.append(r)
+        kk, vv = rows
+        grp = self.Hq // hkv
+        qh = q.view(hkv, grp, d)
+        s = torch.einsum("hgd,thd->hgt", qh, kk) * self.scale
+        p = torch.softmax(s, dim=-1)
+        return torch.einsum("hgt,thd->hgd", p, vv).reshape(self.Hq, d)
 
     def bytes_per_layer_token(self, total_tokens: int) -> int:
         """Algorithmic HBM bytes of one fused decode launch attending

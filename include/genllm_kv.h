@@ -274,12 +274,25 @@ int gkv_gather_create(int device, int world, int rank, int max_layers, void* con
                       uint32_t* const* flag_bases, gkv_gather** out);
 int gkv_gather_destroy(gkv_gather* g);
 
+/* The limit of the wait for the peers' blocks (default 1 s; 1 us to 10 s).
+ * When it runs out the combine stops waiting, sets bit 1 of the device
+ * error word (gkv_check_device_errors) and finishes, so the stream stays
+ * usable; the output then lacks the missing peers' blocks. */
+int gkv_gather_set_wait_limit(gkv_gather* g, uint64_t limit_ns);
+
 /* One decode step of this rank's heads (as gkv_paged_attention with
  * seq_len 1, causal), whose [n_q_heads][128] output block lands in EVERY
  * rank's region at out_offset + rank * n_q_heads * 128 * elem bytes. The
  * launch completes only once all ranks' blocks for this layer and step have
- * arrived in this rank's region (a bounded wait, 1 s; on timeout the device
- * error word gets bit 1). Every rank must make the same sequence of calls. */
+ * arrived in this rank's region (a bounded wait, gkv_gather_set_wait_limit;
+ * on timeout the device error word gets bit 1). Every rank must make the same
+ * sequence of calls. A layer's blocks stay in place until that layer's next
+ * call on any rank: a peer's next call for the layer stores over them as
+ * soon as that peer gets there, so read the region (stream-ordered) before
+ * this rank's next call for the same layer. With two or more layers called
+ * in turn every rank waits for the others at each layer, which keeps peers
+ * from running a whole step ahead; with a single layer, copy the output out
+ * before the next call. */
 int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, const void* K,
                                const void* V, gkv_gather* g, size_t out_offset, int32_t n_q_heads,
                                float scale, int32_t out_dtype, gkv_stream_t stream);
@@ -304,11 +317,20 @@ int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, 
  * device; make that first call before any stream capture. All calls share
  * the one scratch array (it keeps the previous call's contents), so calls
  * that overlap on the GPU — other streams, other threads — race; order them.
- * The device error word is cleared at the start of each call. */
+ * The device error word is cleared at the start of each call; read it with
+ * gkv_paged_decode_static_scratch_errors. */
 int gkv_paged_decode_static_scratch(const gkv_pool_desc* pool, const int32_t* device_table,
                                     int32_t n_prior, const void* Q, const void* K, const void* V,
                                     void* out, int32_t n_q_heads, float scale, int32_t out_dtype,
                                     gkv_stream_t stream);
+
+/* No counterpart in the reference. The device error word of the last
+ * gkv_paged_decode_static_scratch call on the current device, after the
+ * stream's work has finished (this call synchronises `stream`): bit 0 = a
+ * page id in device_table outside [0, pool_pages) (that page was skipped, so
+ * the output is wrong), bit 1 = a bounded wait ran out. Allocates nothing;
+ * the word stays as it is until the next decode call clears it. */
+int gkv_paged_decode_static_scratch_errors(uint32_t* flags, gkv_stream_t stream);
 
 /* ---------------- QK-norm + RoPE (the step feeding the append) -------------
  * Qwen3's attention block turns the Q/K/V projections [S][H*128] into the

@@ -8,7 +8,7 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = "/root/reference"
+REF = os.environ.get("GENLLM_REF") or os.path.join(os.path.dirname(ROOT), "reference")
 
 
 @pytest.mark.skipif(not os.path.isdir(REF) or not shutil.which("g++"), reason="reference tree absent")

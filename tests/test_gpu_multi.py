@@ -179,3 +179,65 @@ def test_fused_head_allgather_two_gpus():
     for p in ps:
         p.join(timeout=60)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def test_gather_wait_runs_out_and_stream_stays_usable():
+    """The fused gather's wait for its peers is bounded. One GPU, a world-2
+    gather whose 'peer' never runs: both regions are local buffers, so this
+    rank's combine stores its block into both and publishes its flag, but the
+    peer's flag slot is never written. With a 2 ms limit the combine gives up,
+    sets the timeout bit of the error word and finishes; the stream keeps
+    working, and this rank's own block is still correct."""
+    import ctypes as C
+
+    from genllm_b200 import _lib
+    from genllm_b200.synth import fragmented_case, randn_bf16
+    from gpu_util import assert_close, build_state, to_dev_bf16
+
+    L = _lib.lib()
+    hq, hkv, d = 8, 4, 128
+    case = fragmented_case(91, hq, hkv, d, 300, 40)
+    m = build_state(case)
+    ref = build_state(case)  # the same cache, decoded without the gather
+    bases, flags = (C.c_void_p * 2)(), (C.c_void_p * 2)()
+    for r in range(2):
+        b, f = C.c_void_p(), C.c_void_p()
+        assert L.gkv_device_alloc(0, hq * d * 2 * 2, C.byref(b)) == 0
+        assert L.gkv_device_alloc(0, 4 * 2, C.byref(f)) == 0
+        bases[r], flags[r] = b, f
+    g = C.c_void_p()
+    assert L.gkv_gather_create(0, 2, 0, 1, bases, flags, C.byref(g)) == 0, L.gkv_last_error()
+    assert L.gkv_gather_set_wait_limit(g, 2_000_000) == 0
+    assert L.gkv_gather_set_wait_limit(g, 10) == _lib.GKV_ERR_INVALID
+    rng = np.random.default_rng(2)
+    q = to_dev_bf16(randn_bf16(rng, (hq, 1, d)), "cuda")
+    k = to_dev_bf16(randn_bf16(rng, (hkv, 1, d)), "cuda")
+    v = to_dev_bf16(randn_bf16(rng, (hkv, 1, d)), "cuda")
+    s = torch.cuda.current_stream()
+    st = L.gkv_paged_attention_gather(m.handle, 0, C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                                      C.c_void_p(v.data_ptr()), g, 0, hq, C.c_float(case.scale), _lib.GKV_F32,
+                                      C.c_void_p(s.cuda_stream))
+    assert st == 0, L.gkv_last_error()
+    torch.cuda.synchronize()
+    assert m.check_device_errors(0) & 2, "the wait for the silent peer did not report a timeout"
+    # The stream and the context are fine: a regular decode and a torch op run after it.
+    from genllm_b200.paged_attention import paged_attention
+    want = torch.empty(1, hq, 1, d, device="cuda")
+    paged_attention(ref, 0, q.view(1, hq, 1, d), k.view(1, hkv, 1, d), v.view(1, hkv, 1, d), out=want,
+                    scale=case.scale)
+    torch.cuda.synchronize()
+    # Rank 0's block sits at offset 0 of its own region (bases[0]).
+    got = torch.as_tensor(_CudaView(bases[0], hq * d), device="cuda").clone()  # ctypes array items are ints
+    torch.cuda.synchronize()
+    assert_close(got.view(hq, d).cpu().numpy(), want[0, :, 0].cpu().numpy(), "own block after timeout")
+    assert ref.check_device_errors(0) == 0
+    assert L.gkv_gather_destroy(g) == 0
+    for r in range(2):
+        L.gkv_device_free(0, bases[r])
+        L.gkv_device_free(0, flags[r])
+
+
+class _CudaView:
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (n,), "typestr": "<f4", "version": 3,
+                                         "strides": None}

@@ -2,7 +2,7 @@
 oracle, through the public API: the standalone fused kernel bit-exact, and
 the attention op on the projections (decode: fused into the decode kernel;
 chunks: fused kernel + prefill) with the appended pages bit-exact and the
-output within |got - want| <= 2e-3 + 1e-2*|want|."""
+output within max-abs 2e-3 and max-rel 1e-2 (gpu_util.assert_close)."""
 import dataclasses
 import os
 import sys
