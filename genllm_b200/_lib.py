@@ -90,6 +90,10 @@ SIGNATURES = {
     "gkv_gather_create": ([C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp)], C.c_int),
     "gkv_gather_destroy": ([vp], C.c_int),
     "gkv_gather_set_wait_limit": ([vp, C.c_uint64], C.c_int),
+    "gkv_nccl_unique_id": ([vp], C.c_int),
+    "gkv_nccl_comm_create": ([C.c_int, C.c_int, C.c_int, vp, C.POINTER(vp)], C.c_int),
+    "gkv_nccl_comm_destroy": ([vp], C.c_int),
+    "gkv_allgather_heads": ([vp, vp, vp, C.c_size_t, vp], C.c_int),
     "gkv_paged_attention_gather": ([vp, i32, vp, vp, vp, vp, C.c_size_t, i32, C.c_float, i32, vp], C.c_int),
     "gkv_paged_decode_static_scratch": ([C.POINTER(PoolDesc), vp, i32, vp, vp, vp, vp, i32, C.c_float, i32, vp],
                                         C.c_int),

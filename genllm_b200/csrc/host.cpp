@@ -12,6 +12,7 @@
 //     unchanged, where the reference keeps counting tokens and later indexes
 //     its table out of bounds (page_attention.cpp:155,161,127);
 //   * all work is enqueued on the caller's stream; nothing synchronises.
+#include <nvtx3/nvToolsExt.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -177,6 +178,16 @@ bool encode_q_map_sw128(const uint16_t* q, int32_t n_q_heads, int32_t seq_len, C
 }  // namespace gkv
 
 // ============================ raw tier ======================================
+
+// NVTX range around a host entry point (the launches it enqueues): names
+// the path's phases (append, decode, merge, gather, export) in a timeline
+// profiler; a no-op unless a tool is attached.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 struct gkv_table {
     int device = 0;
@@ -410,6 +421,7 @@ int gkv_table_check_errors(gkv_table* t, uint32_t* flags) {
 
 int gkv_append_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
                       const void* K, const void* V, int32_t seq_len, gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv append");
     int st = check_pool(pool);
     if (st) return st;
     if (!t || n_prior < 0 || seq_len < 0) return fail(GKV_ERR_INVALID, "gkv_append_kv_raw: bad arguments");
@@ -436,6 +448,7 @@ int check_format_buffers(int32_t format, const void* K, const void* V, const voi
 
 int gkv_export_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_tokens, int32_t format, void* K_out,
                       void* V_out, float* k_scales, float* v_scales, gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv export");
     int st = check_pool(pool);
     if (st) return st;
     if (!t || n_tokens < 0) return fail(GKV_ERR_INVALID, "gkv_export_kv_raw: bad arguments");
@@ -458,6 +471,7 @@ int gkv_export_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_tokens,
 int gkv_import_kv_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
                       int32_t format, const void* K_in, const void* V_in, const float* k_scales,
                       const float* v_scales, int32_t seq_len, gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv import");
     if (format == GKV_KV_BF16) return gkv_append_kv_raw(pool, t, n_prior, np, K_in, V_in, seq_len, stream);
     int st = check_pool(pool);
     if (st) return st;
@@ -545,6 +559,7 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
                      pool->pool_pages, pool->n_kv_heads};
 
     if (seq_len == 1) {
+        NvtxRange nvtx_range("gkv decode (append + attention + split merge)");
         if (pool->n_kv_heads > 8)
             return fail(GKV_ERR_UNSUPPORTED, "decode kernel built for at most 8 kv heads per GPU (got %d)",
                         pool->n_kv_heads);
@@ -580,7 +595,11 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
         return GKV_OK;
     }
 
-    if ((st = append_chunks(pool, t, n_prior, np, K, V, seq_len, s))) return st;
+    {
+        NvtxRange nvtx_range("gkv chunk append");
+        if ((st = append_chunks(pool, t, n_prior, np, K, V, seq_len, s))) return st;
+    }
+    NvtxRange nvtx_range("gkv chunk attention");
     gkv::PrefillLaunch pl{};
     pl.q = static_cast<const uint16_t*>(Q);
     pl.out = out;
@@ -643,6 +662,7 @@ int gkv_rope_cache(float theta, int32_t head_dim, int32_t max_seq, float* cos_ou
 int gkv_qk_norm_rope(const void* q_flat, const void* k_flat, const void* v_flat, int32_t seq_len, int32_t n_q_heads,
                      int32_t n_kv_heads, const gkv_qk_norm* qk, int32_t start_pos, void* q_out, void* k_out,
                      void* v_out, gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv qk-norm + rope");
     if (!q_flat || !k_flat || !v_flat || !q_out || !k_out || !v_out || seq_len < 0 || n_q_heads < 1 || n_kv_heads < 1)
         return fail(GKV_ERR_INVALID, "gkv_qk_norm_rope: bad arguments");
     if (!aligned16(v_flat) || !aligned16(v_out)) return fail(GKV_ERR_INVALID, "V buffers must be 16-byte aligned");
@@ -1056,6 +1076,7 @@ int gkv_paged_attention_qknorm(gkv_manager* m, int32_t layer_id, const void* q_f
 int gkv_decode_layers(gkv_manager* m, int32_t n_layers, const int32_t* layer_ids, const void* const* Q,
                       const void* const* K, const void* const* V, void* const* out, int32_t n_q_heads, float scale,
                       int32_t out_dtype, gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv decode step (multi-layer)");
     if (!m || n_layers < 0 || (n_layers && (!layer_ids || !Q || !K || !V || !out)))
         return fail(GKV_ERR_INVALID, "gkv_decode_layers: bad arguments");
     bool distinct = true;
@@ -1256,6 +1277,7 @@ int gkv_decode_graph_create(gkv_manager* m, int32_t n_layers, const int32_t* lay
 }
 
 int gkv_decode_graph_step(gkv_decode_graph* g, gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv decode step (captured)");
     if (!g) return fail(GKV_ERR_INVALID, "null decode graph");
     DeviceGuard dg(g->device);
     if (!dg.ok()) return fail(GKV_ERR_CUDA, "cannot select device %d", g->device);
@@ -1626,6 +1648,7 @@ int gkv_gather_destroy(gkv_gather* gg) {
 int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, const void* K, const void* V,
                                gkv_gather* gg, size_t out_offset, int32_t n_q_heads, float scale, int32_t out_dtype,
                                gkv_stream_t stream) {
+    NvtxRange nvtx_range("gkv decode + head all-gather");
     if (!gg) return fail(GKV_ERR_INVALID, "null gather");
     if (layer_id < 0 || layer_id >= gg->max_layers) return fail(GKV_ERR_INVALID, "layer %d beyond the gather's %d",
                                                              layer_id, gg->max_layers);

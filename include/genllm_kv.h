@@ -274,6 +274,20 @@ int gkv_gather_create(int device, int world, int rank, int max_layers, void* con
                       uint32_t* const* flag_bases, gkv_gather** out);
 int gkv_gather_destroy(gkv_gather* g);
 
+/* The same all-gather over NCCL, for hosts that shard without the IPC tier
+ * (the reference has no multi-GPU attention; its devices exchange layer
+ * outputs through host copies, src/backend/cuda/memcpy.cu:29-44). After each
+ * rank's decode step of its Hkv / N heads (gkv_paged_attention with
+ * n_q_heads = Hq / N), gkv_allgather_heads gathers the ranks' output blocks
+ * [Hq / N][128] (bytes_per_rank each) into full, rank-major, on `stream`.
+ * NCCL is loaded at run time (libnccl.so.2, or $GKV_NCCL_LIB); a
+ * communicator passed in must come from that same library (or from
+ * gkv_nccl_comm_create). Without NCCL these return GKV_ERR_UNSUPPORTED. */
+int gkv_nccl_unique_id(void* id /* 128 bytes, rank 0 creates it and sends it to the others */);
+int gkv_nccl_comm_create(int device, int world, int rank, const void* id, void** comm);
+int gkv_nccl_comm_destroy(void* comm);
+int gkv_allgather_heads(void* comm, const void* local, void* full, size_t bytes_per_rank, gkv_stream_t stream);
+
 /* The limit of the wait for the peers' blocks (default 1 s; 1 us to 10 s).
  * When it runs out the combine stops waiting, sets bit 1 of the device
  * error word (gkv_check_device_errors) and finishes, so the stream stays

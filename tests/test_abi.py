@@ -2,6 +2,8 @@
 import os
 import re
 
+import pytest
+
 from genllm_b200 import _lib
 
 HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "genllm_kv.h")
@@ -90,3 +92,18 @@ def test_decode_graph_entry_points_reject_bad_arguments_without_a_gpu():
     assert L.gkv_decode_graph_create(m, 1, ids, ptrs, ptrs, ptrs, ptrs, 8, 0.1, 30, None, C.byref(g)) == \
         _lib.GKV_ERR_STATE
     assert L.gkv_manager_destroy(m) == 0
+
+
+def test_nccl_unique_id_through_the_c_abi():
+    """The NCCL tier opens libnccl at run time; making a unique id needs no
+    GPU, so this checks the loading and the call path on the CPU."""
+    import ctypes as C
+    from genllm_b200 import _lib
+    L = _lib.lib()
+    uid = (C.c_char * 128)()
+    st = L.gkv_nccl_unique_id(uid)
+    if st == _lib.GKV_ERR_UNSUPPORTED:
+        pytest.skip("no libnccl.so.2 on this machine")
+    assert st == 0, L.gkv_last_error()
+    assert any(bytes(uid)), "unique id left empty"
+    assert L.gkv_nccl_unique_id(None) == _lib.GKV_ERR_INVALID

@@ -24,7 +24,10 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode="p2p"):
+    """mode "p2p": the gather fused into the decode (HeadGather); "nccl": a
+    plain decode of the rank's heads, then gkv_allgather_heads over a NCCL
+    communicator made through the C ABI (gkv_nccl_unique_id / comm_create)."""
     try:
         import sys
         here = os.path.dirname(os.path.abspath(__file__))
@@ -41,7 +44,21 @@ def _worker(rank, world, port, q):
         from oracle.oracle import Oracle, OraclePool
         hq, hkv, d = 16, 8, 128
         qb, qe, kb, ke = shard_heads(hq, hkv, world, rank)
-        hg = HeadGather(rank, n_layers=2, n_q_heads=hq)
+        import ctypes as C
+        from genllm_b200 import _lib
+        from genllm_b200.paged_attention import paged_attention
+        L = _lib.lib()
+        if mode == "p2p":
+            hg = HeadGather(rank, n_layers=2, n_q_heads=hq)
+        else:
+            uid = (C.c_char * 128)()
+            if rank == 0:
+                assert L.gkv_nccl_unique_id(uid) == 0, L.gkv_last_error()
+            box = [bytes(uid)]
+            dist.broadcast_object_list(box, src=0)
+            comm = C.c_void_p()
+            assert L.gkv_nccl_comm_create(rank, world, rank, box[0], C.byref(comm)) == 0, L.gkv_last_error()
+            full_out = torch.empty(hq, d, dtype=torch.bfloat16, device="cuda")
         orc = Oracle()
         mgrs_cases = []
         from genllm_b200.paged_attention import PagedAttentionManager
@@ -71,7 +88,14 @@ def _worker(rank, world, port, q):
                 Q = to_dev_bf16(np.ascontiguousarray(qf[qb:qe]), "cuda").view(1, qe - qb, 1, d)
                 K = to_dev_bf16(np.ascontiguousarray(kf[kb:ke]), "cuda").view(1, ke - kb, 1, d)
                 V = to_dev_bf16(np.ascontiguousarray(vf[kb:ke]), "cuda").view(1, ke - kb, 1, d)
-                out = hg.decode(m, layer, Q, K, V, full.scale)
+                if mode == "p2p":
+                    out = hg.decode(m, layer, Q, K, V, full.scale)
+                else:
+                    mine = paged_attention(m, layer, Q, K, V, scale=full.scale)  # [1, Hq/N, 1, D] bf16
+                    st = L.gkv_allgather_heads(comm, C.c_void_p(mine.data_ptr()), C.c_void_p(full_out.data_ptr()),
+                                               mine.numel() * 2, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+                    assert st == 0, L.gkv_last_error()
+                    out = full_out
                 torch.cuda.synchronize()
                 op.append_kv(kp, vp, kf, vf, hkv, 1, d)
                 k_ids, v_ids = op.table()
@@ -81,7 +105,10 @@ def _worker(rank, world, port, q):
                 assert_close(got, bf16_to_f32(orc.round_bf16(want[:, 0])), f"rank {rank} step {step} layer {layer}")
         assert m.check_device_errors(0) == 0 and m.check_device_errors(1) == 0
         dist.barrier()
-        hg.close()
+        if mode == "p2p":
+            hg.close()
+        else:
+            assert L.gkv_nccl_comm_destroy(comm) == 0
         dist.destroy_process_group()
         q.put((rank, "ok"))
     except Exception as e:  # report to the parent
@@ -168,11 +195,12 @@ def test_fused_head_allgather_back_to_back_steps():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_head_allgather_two_gpus():
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+def test_head_allgather_two_gpus(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in ps:
         p.start()
     res = dict(q.get(timeout=300) for _ in ps)
