@@ -49,10 +49,13 @@ def parse():
     ap.add_argument("--pool", type=int, default=0, help="pages per pool (0: max(4096, ctx/16 + 64))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qknorm", "flash", "export"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "qknorm", "flash", "export", "append", "qkrope"],
                     help="decode: config 3 (the headline line); prefill: config 4, chunked prefill on tensor "
                          "cores; qknorm: config 3 fed the Q/K/V projections, QK-norm + RoPE fused into the step; "
-                         "export: config 3's 36 layers exported to head-major e4m3 (KV format row)")
+                         "export: config 3's 36 layers exported to head-major e4m3 (KV format row); append: the "
+                         "chunk append kernel alone (8192 tokens in 512-token chunks into 36 layers' pages); "
+                         "qkrope: the standalone QK-norm + RoPE + permute kernel on 512-token chunks")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="N>1: head all-gather fused into the decode (NVLink peer stores) or NCCL all_gather")
     ap.add_argument("--no-kernel-events", action="store_true",
@@ -656,6 +659,165 @@ def run_qknorm(args):
     print(json.dumps(line), flush=True)
 
 
+def run_append(args):
+    """The chunk append (append_kv_from_tensor, src/core/page_attention.cpp:
+    104-139) alone: Qwen3-1.7B KV shape (Hkv 8, D 128, bf16), an 8192-token
+    prompt appended in 512-token chunks into each of 36 layers' fragmented
+    pools (a step = 36 x 16 launches of kv_append_kernel). Inputs (36 x 32 MiB
+    of K and V) and pools exceed L2. Metric: algorithmic HBM GB/s (K and V
+    read once, written once, plus the published table entries)."""
+    import torch
+    from genllm_b200.paged_attention import PagedAttentionManager
+
+    torch.cuda.set_device(0)
+    L, hkv, d, chunk, prompt = args.layers, 8, 128, 512, 8192
+    dev = torch.device("cuda", 0)
+    m = PagedAttentionManager(0)
+    g = torch.Generator(device=dev).manual_seed(12)
+    K, V = [], []
+    for l in range(L):
+        m.init_layer(l, hkv, d)
+        m.reserve_layer(l, prompt // 16 + 64)
+        K.append(torch.randn(hkv, prompt, d, generator=g, device=dev).to(torch.bfloat16))
+        V.append(torch.randn(hkv, prompt, d, generator=g, device=dev).to(torch.bfloat16))
+    n_chunks = prompt // chunk
+    Kc = [[K[l][:, c * chunk:(c + 1) * chunk].contiguous() for c in range(n_chunks)] for l in range(L)]
+    Vc = [[V[l][:, c * chunk:(c + 1) * chunk].contiguous() for c in range(n_chunks)] for l in range(L)]
+    del K, V
+    stream = torch.cuda.current_stream()
+
+    def launches():
+        for l in range(L):
+            for c in range(n_chunks):
+                m.append_kv_from_tensor(l, Kc[l][c], Vc[l][c])
+
+    def step():
+        m.reset()
+        launches()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    # The same launches captured once (pages allocated at capture) and
+    # replayed: device time without the host's per-call cost, which is
+    # larger than one 4 MiB launch.
+    m.reset()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        launches()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms_graph = t0.elapsed_time(t1) / args.steps
+    launch_ms = ms_graph / (L * n_chunks)
+    per_launch = 2 * 2 * hkv * chunk * d * 2 + (chunk // 16) * 8
+    gbs = per_launch * L * n_chunks / (ms / 1e3) / 1e9
+    peak, src = measured_peak()
+    achieved = per_launch / (launch_ms / 1e3) / 1e9
+    line = {"metric": "KV chunk append (append_kv_from_tensor) algorithmic HBM GB/s, Qwen3-1.7B KV shape",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "8192-token prompt appended in 512-token chunks into 36 layers' pages",
+                       "layers": L, "n_kv_heads": hkv, "head_dim": d, "chunk": chunk,
+                       "l2": "36 x 32 MiB of inputs per step, larger than L2"},
+            "gpu_launches": L * n_chunks * args.steps,
+            "captured_step_ms": round(ms_graph, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None, "peak_source": src,
+                         "kernel": "kv_append_kernel", "bytes_per_launch": per_launch,
+                         "launch_us": round(launch_ms * 1e3, 3),
+                         "how": "mean per launch of the step's 576 launches replayed from a CUDA graph"},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+def run_qkrope(args):
+    """The standalone QK-norm + RoPE + head-major permute (gkv_qk_norm_rope;
+    src/model/Qwen3.cpp:136-154 as one launch instead of seven): Qwen3-4B
+    shape (Hq 32, Hkv 8), 512-token chunks at positions 0..511, distinct
+    inputs for 36 layers (36 x 6 MiB, larger than L2). Metric: algorithmic
+    HBM GB/s (projections read, the three head-major outputs written, the
+    position's cos/sin rows read once per launch)."""
+    import torch
+    from genllm_b200.paged_attention import QkNorm, qk_norm_rope
+
+    torch.cuda.set_device(0)
+    L, hq, hkv, d, S = args.layers, HQ, HKV, D, 512
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(13)
+    qk = QkNorm(1 + 0.25 * torch.randn(d), 1 + 0.25 * torch.randn(d), 1e-6, 1e6, S, 0)
+    ins = [tuple(torch.randn(S, h * d, generator=g, device=dev).to(torch.bfloat16) for h in (hq, hkv, hkv))
+           for _ in range(L)]
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for l in range(L):
+            qk_norm_rope(*ins[l], hq, hkv, qk, 0)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms_graph = t0.elapsed_time(t1) / args.steps
+    launch_ms = ms_graph / L
+    per_launch = 2 * S * (hq + 2 * hkv) * d * 2 + 2 * S * d * 4 + 2 * d * 4
+    gbs = per_launch * L / (ms / 1e3) / 1e9
+    peak, src = measured_peak()
+    achieved = per_launch / (launch_ms / 1e3) / 1e9
+    line = {"metric": "QK-norm + RoPE + permute (one launch) algorithmic HBM GB/s, Qwen3-4B shape, 512-token chunks",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "gkv_qk_norm_rope on a 512-token chunk for each of 36 layers",
+                       "layers": L, "n_q_heads": hq, "n_kv_heads": hkv, "head_dim": d, "chunk": S,
+                       "l2": "36 x 6 MiB of projections per step, larger than L2"},
+            "gpu_launches": L * args.steps,
+            "captured_step_ms": round(ms_graph, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None, "peak_source": src,
+                         "kernel": "qk_norm_rope_kernel", "bytes_per_launch": per_launch,
+                         "launch_us": round(launch_ms * 1e3, 3),
+                         "how": "mean per launch of the step's 36 launches replayed from a CUDA graph"},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -676,6 +838,12 @@ def main():
         return
     if args.workload == "export":
         run_export(args)
+        return
+    if args.workload == "append":
+        run_append(args)
+        return
+    if args.workload == "qkrope":
+        run_qkrope(args)
         return
 
     import torch

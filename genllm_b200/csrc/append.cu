@@ -3,9 +3,9 @@
 // Replaces the reference's per-(token, head) synchronous cudaMemcpy loop
 // (src/core/page_attention.cpp:122-139): token p of head h, a 256-byte row
 // of K[h][p][:], lands at page(table[(n_prior+p)/16]) + ((n_prior+p)%16 * Hkv
-// + h) * 128 elements, in K's pool; the same for V. Each thread moves 16-byte
-// units ordered so that consecutive threads write consecutive bytes of a
-// page slot ([Hkv][128] contiguous). Pure byte copy: bit-exact by design.
+// + h) * 128 elements, in K's pool; the same for V. A warp fills one page
+// slot ([Hkv][128] contiguous) with 16-byte units, consecutive lanes on
+// consecutive bytes. Pure byte copy: bit-exact by design.
 #include "device.cuh"
 #include "kernels.h"
 
@@ -30,36 +30,59 @@ struct AppendParams {
     int2 new_ids[kMaxNewPagesPerLaunch];
 };
 
-__global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams a) {
+constexpr int kAppendWarps = 4;
+
+// One warp per (token, K|V): the token's Hkv rows (one per head, src_len
+// rows apart in the input) land in one contiguous page slot [Hkv][128]. Each
+// lane loads its 16-byte units of the slot before the table entry is known
+// (the source does not depend on it), so the two latencies overlap; then it
+// stores them in slot order (consecutive lanes, consecutive bytes).
+__global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const AppendParams a) {
     if (blockIdx.x == 0 && (int)threadIdx.x < a.new_n)
         a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
 
     constexpr int kUnitsPerRow = kHeadDim * 2 / 16;  // 16-byte units in a 256-byte row
+    constexpr int kBatch = 4;                        // units per lane in flight
+    const int lane = threadIdx.x & 31;
     const int Hkv = a.n_kv_heads;
-    const long long units = 2ll * a.count * Hkv * kUnitsPerRow;
-    for (long long u = blockIdx.x * (long long)blockDim.x + threadIdx.x; u < units;
-         u += (long long)gridDim.x * blockDim.x) {
-        const int d16 = (int)(u % kUnitsPerRow);
-        long long r = u / kUnitsPerRow;
-        const int h = (int)(r % Hkv);
-        r /= Hkv;
-        const int p = a.p_begin + (int)(r % a.count);
-        const int which = (int)(r / a.count);  // 0 = K, 1 = V
+    const int units = Hkv * kUnitsPerRow;            // units of one page slot
+    const int n_items = 2 * a.count;
+    for (int w = blockIdx.x * kAppendWarps + (int)(threadIdx.x >> 5); w < n_items; w += gridDim.x * kAppendWarps) {
+        const int which = w & 1;  // 0 = K, 1 = V
+        const int p = a.p_begin + (w >> 1);
         const int pos = a.n_prior + p;
         const int lp = pos / kPageSlots;
         const int slot = pos % kPageSlots;
-        const int rr = lp - a.new_first;
-        const int2 e = (rr >= 0 && rr < a.new_n) ? a.new_ids[rr] : a.table[lp];
-        const int page = which ? e.y : e.x;
-        if (page < 0 || page >= a.pool_pages) {
-            atomicOr(a.err, kErrBadPage);
-            continue;
+        int page = 0;
+        if (lane == 0) {
+            const int rr = lp - a.new_first;
+            const int2 e = (rr >= 0 && rr < a.new_n) ? a.new_ids[rr] : a.table[lp];
+            page = which ? e.y : e.x;
         }
         const uint4* src = which ? a.v : a.k;
         uint4* dst = which ? a.v_base : a.k_base;
-        const size_t s_idx = ((size_t)h * a.src_len + p) * kUnitsPerRow + d16;
-        const size_t d_idx = (((size_t)page * kPageSlots + slot) * Hkv + h) * kUnitsPerRow + d16;
-        dst[d_idx] = __ldg(src + s_idx);
+        for (int u0 = 0; u0 < units; u0 += 32 * kBatch) {
+            uint4 buf[kBatch];
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int j = u0 + b * 32 + lane;
+                if (j < units) {
+                    const int h = j / kUnitsPerRow, d16 = j % kUnitsPerRow;
+                    buf[b] = __ldg(src + ((size_t)h * a.src_len + p) * kUnitsPerRow + d16);
+                }
+            }
+            const int pg = __shfl_sync(0xFFFFFFFFu, page, 0);
+            if (pg < 0 || pg >= a.pool_pages) {
+                if (lane == 0 && u0 == 0) atomicOr(a.err, kErrBadPage);
+                continue;
+            }
+            uint4* slot_base = dst + ((size_t)pg * kPageSlots + slot) * units;
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int j = u0 + b * 32 + lane;
+                if (j < units) slot_base[j] = buf[b];
+            }
+        }
     }
 }
 
@@ -85,11 +108,10 @@ cudaError_t launch_append(const PoolView& pool, int2* table, const NewPages& np,
     a.new_first = np.first;
     a.new_n = np.n;
     for (int i = 0; i < np.n; ++i) a.new_ids[i] = np.ids[i];
-    const long long units = 2ll * a.count * pool.n_kv_heads * (kHeadDim * 2 / 16);
-    long long blocks = (units + 255) / 256;
+    long long blocks = (2ll * a.count + kAppendWarps - 1) / kAppendWarps;
     if (blocks < 1) blocks = 1;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    kv_append_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a);
+    kv_append_kernel<<<(unsigned)blocks, kAppendWarps * 32, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -144,6 +144,17 @@ __device__ __forceinline__ uint16_t bf16_bits_ref(float f) {
     return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
+// The same bits as bf16_bits_ref with fewer instructions: for normal fp32
+// values the reference's rounding is round-to-nearest-even, which is the
+// hardware conversion; zero exponents (flushed to a signed zero) and
+// infinities / NaNs take the reference's path.
+__device__ __forceinline__ uint16_t bf16_bits_ref_fast(float f) {
+    const uint32_t u = __float_as_uint(f);
+    const uint32_t e = u & 0x7F800000u;
+    if (e == 0u || e == 0x7F800000u) return bf16_bits_ref(f);
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
 // Store one fp32 output element in the requested dtype (reference codes).
 __device__ __forceinline__ void store_out(void* out, size_t idx, float v, int dtype) {
     if (dtype == 0) {

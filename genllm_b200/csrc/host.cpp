@@ -665,7 +665,11 @@ int gkv_qk_norm_rope(const void* q_flat, const void* k_flat, const void* v_flat,
     NvtxRange nvtx_range("gkv qk-norm + rope");
     if (!q_flat || !k_flat || !v_flat || !q_out || !k_out || !v_out || seq_len < 0 || n_q_heads < 1 || n_kv_heads < 1)
         return fail(GKV_ERR_INVALID, "gkv_qk_norm_rope: bad arguments");
-    if (!aligned16(v_flat) || !aligned16(v_out)) return fail(GKV_ERR_INVALID, "V buffers must be 16-byte aligned");
+    if (!aligned16(q_flat) || !aligned16(k_flat) || !aligned16(v_flat) || !aligned16(q_out) || !aligned16(k_out) ||
+        !aligned16(v_out))
+        return fail(GKV_ERR_INVALID, "gkv_qk_norm_rope: every buffer must be 16-byte aligned");
+    if (n_q_heads + n_kv_heads > 96)
+        return fail(GKV_ERR_UNSUPPORTED, "gkv_qk_norm_rope: at most 96 query + kv heads per token");
     int st = check_qk(qk, start_pos, seq_len);
     if (st) return st;
     const gkv::QkNorm n{qk->q_norm_w, qk->k_norm_w, qk->cos_tab, qk->sin_tab, qk->eps};

@@ -64,8 +64,8 @@ __device__ __forceinline__ void norm_rope_row(const float (&x)[4], const RowPara
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
         const float c = p.c[it], s = p.s[it];
-        out[it] = bf16_bits_ref(__fmaf_rn(y[it], c, -__fmul_rn(y[it + 2], s)));
-        out[it + 2] = bf16_bits_ref(__fmaf_rn(y[it], s, __fmul_rn(y[it + 2], c)));
+        out[it] = bf16_bits_ref_fast(__fmaf_rn(y[it], c, -__fmul_rn(y[it + 2], s)));
+        out[it + 2] = bf16_bits_ref_fast(__fmaf_rn(y[it], s, __fmul_rn(y[it + 2], c)));
     }
 }
 
@@ -123,8 +123,8 @@ __device__ __forceinline__ void norm_rope_row_g8(const float (&x)[4][4], int j, 
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const float c = p.c[it][k], s = p.s[it][k];
-            out[it][k] = bf16_bits_ref(__fmaf_rn(y[it][k], c, -__fmul_rn(y[it + 2][k], s)));
-            out[it + 2][k] = bf16_bits_ref(__fmaf_rn(y[it][k], s, __fmul_rn(y[it + 2][k], c)));
+            out[it][k] = bf16_bits_ref_fast(__fmaf_rn(y[it][k], c, -__fmul_rn(y[it + 2][k], s)));
+            out[it + 2][k] = bf16_bits_ref_fast(__fmaf_rn(y[it][k], s, __fmul_rn(y[it + 2][k], c)));
         }
 }
 

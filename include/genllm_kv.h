@@ -375,7 +375,7 @@ int gkv_rope_cache(float theta, int32_t head_dim, int32_t max_seq, float* cos_ou
  * Replaces ApplyRopeImpl<CUDA>::execute (src/backend/cuda/rope.cu:52-111),
  * RmsNormImpl<CUDA>::execute (src/backend/cuda/normalization.cu:49-90) on
  * the heads and PermuteImpl<CUDA>::execute (src/backend/cuda/shape.cu:45) x3.
- * Allocates nothing. */
+ * All six buffers 16-byte aligned; Hq + Hkv <= 96. Allocates nothing. */
 int gkv_qk_norm_rope(const void* q_flat, const void* k_flat, const void* v_flat, int32_t seq_len,
                      int32_t n_q_heads, int32_t n_kv_heads, const gkv_qk_norm* qk, int32_t start_pos,
                      void* q_out, void* k_out, void* v_out, gkv_stream_t stream);

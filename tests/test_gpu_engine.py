@@ -64,8 +64,14 @@ def runs(tmp_path_factory):
         summary = json.loads([l for l in r.stdout.splitlines() if l.startswith("{\"prompt_len\"")][-1])
         out[n] = (summary, *_read(res))
     os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
+    summary = {n: {k: v for k, v in s.items() if k != "tokens"} for n, (s, _, _) in out.items()}
+    for a, b in (("engine_cuda_b200", "engine_cuda_ref"), ("engine_cuda_b200", "engine_cpu"),
+                 ("engine_cuda_ref", "engine_cpu")):
+        summary[f"{a} vs {b}"] = {f"pos{i}_max_abs_logit_diff": float(np.abs(out[a][2][i] - out[b][2][i]).max())
+                                  for i in DUMPS}
+        summary[f"{a} vs {b}"]["argmax_agree"] = int(sum(x[0] == y[0] for x, y in zip(out[a][1], out[b][1])))
     with open(os.path.join(ROOT, "gpurun_out", "engine_config2.json"), "w") as f:
-        json.dump({n: {k: v for k, v in s.items() if k != "tokens"} for n, (s, _, _) in out.items()}, f, indent=1)
+        json.dump(summary, f, indent=1)
     return out
 
 
@@ -81,14 +87,20 @@ def _compare(ref, got, margin_floor):
 
 
 def test_engine_with_b200_attention_matches_genllm_cuda_attention(runs):
-    """Same engine, same CUDA ops; only the paged-attention op differs."""
+    """Same engine, same CUDA ops; only the paged-attention op differs. Its
+    outputs are rounded to bf16 and pass through 28 layers of bf16
+    activations, so the logits move by a few bf16 steps; the swap must move
+    them less than Genllm's own two backends differ from each other."""
     _, rec_ref, rows_ref = runs["engine_cuda_ref"]
     _, rec_b2, rows_b2 = runs["engine_cuda_b200"]
+    _, _, rows_cpu = runs["engine_cpu"]
     agree, checked = _compare(rec_ref, rec_b2, 1.0)
     assert checked > 0.8 * len(rec_ref) and agree == checked, (agree, checked)
     for i in DUMPS:
-        d = np.abs(rows_ref[i] - rows_b2[i])
-        assert d.max() <= 0.02 * rows_ref[i].std() + 1.0, (i, d.max(), rows_ref[i].std())
+        swap = np.abs(rows_ref[i] - rows_b2[i]).max()
+        backends = np.abs(rows_ref[i] - rows_cpu[i]).max()
+        assert swap <= backends, (i, swap, backends)
+        assert np.corrcoef(rows_ref[i], rows_b2[i])[0, 1] > 0.9995, i
 
 
 def test_engine_with_b200_attention_matches_cpu_engine(runs):
