@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--pool", type=int, default=0, help="pages per pool (0: max(4096, ctx/16 + 64))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="skip the config-1 and config-4 side measurements of the default decode line")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "qknorm", "flash", "export", "append", "qkrope"],
@@ -236,8 +238,99 @@ def cpu_step(args):
     return nbytes / dt / 1e9, c["T"], c["kind"], c["sample"], dt, nbytes
 
 
+def measure_config1(args):
+    """Config 1 (Qwen3-0.6B layer: Hq 16, Hkv 8, D 128, 1024 cached tokens in
+    a fragmented 256-page pool, one token appended per step): the decode step
+    through the public API (one call per step) and captured in a CUDA graph
+    (device time), 200 steps each; the reference CPU op timed beside it on
+    the same shape (one thread, its own implementation). Returns a dict for
+    the bench line."""
+    import numpy as np
+    import torch
+    from genllm_b200.paged_attention import DecodeGraph
+    from genllm_b200.workload import DecodeWorkload
+
+    hq, hkv, ctx, pool, n = 16, 8, 1024, 256, 200
+    wl = DecodeWorkload(0, n_layers=1, ctx=ctx, pool_pages=pool, n_q_heads=hq, n_kv_heads=hkv, head_dim=D, seed=0)
+    stream = torch.cuda.current_stream()
+    sh = __import__("ctypes").c_void_p(stream.cuda_stream)
+    for _ in range(5):
+        wl.layer_step(0, sh)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0 = wl.cached(0)
+    e0.record(stream)
+    for _ in range(n):
+        wl.layer_step(0, sh)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    call_us = e0.elapsed_time(e1) * 1e3 / n
+    byts = sum(wl.bytes_per_layer_token(c0 + k + 1) for k in range(n)) / n
+    L0 = wl.layers[0]
+    graph = DecodeGraph(wl.mgr, [0], [L0.q], [L0.k], [L0.v], [L0.out], hq, wl.scale)
+    for _ in range(5):
+        graph.run()
+    torch.cuda.synchronize()
+    c1 = wl.cached(0)
+    e0.record(stream)
+    for _ in range(n):
+        graph.run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    graph_us = e0.elapsed_time(e1) * 1e3 / n
+    gbyts = sum(wl.bytes_per_layer_token(c1 + k + 1) for k in range(n)) / n
+    graph.close()
+    out = {"workload": "config 1: Qwen3-0.6B layer decode, 1024 cached tokens (+1 per step), 256-page fragmented "
+                       "pool, Hq 16 / Hkv 8 / D 128, bf16",
+           "public_api_us_per_step": round(call_us, 3), "public_api_gbs": round(byts / (call_us * 1e-6) / 1e9, 1),
+           "captured_us_per_step": round(graph_us, 3), "captured_gbs": round(gbyts / (graph_us * 1e-6) / 1e9, 1),
+           "bytes_per_step": round(byts)}
+    try:
+        from genllm_b200.synth import bf16_bits
+        from oracle.oracle import RefSession, ref_available
+        if ref_available():
+            s = RefSession(1, hkv, D, pool)
+            tile = bf16_bits(np.random.default_rng(0).standard_normal(1 << 20, dtype=np.float32))
+            for w in (0, 1):
+                view = s.pool_view(0, w).reshape(-1)
+                view[:] = np.resize(tile, view.size)
+                for _ in range(pool):
+                    s.alloc(0, w)
+                for pid in range(pool - 1, ctx // 16 - 1, -1):
+                    s.free(0, w, pid)
+            ids = np.random.default_rng(0).permutation(ctx // 16).astype(np.int32)
+            s.set_table(0, ids, ids, ctx)
+            q = [np.resize(tile, hq * D).reshape(hq, 1, D).copy()]
+            kv = [np.resize(tile[7:], hkv * D).reshape(hkv, 1, D).copy()]
+            o = [np.zeros((hq, 1, D), np.uint16)]
+            reps, t = 0, 0.0
+            while reps < 20:
+                h0 = time.perf_counter()
+                s.paged_attention_layers(q, kv, kv, o, hq, 1, 1 / np.sqrt(D))
+                t += time.perf_counter() - h0
+                reps += 1
+            us = t / reps * 1e6
+            out["cpu_baseline"] = {"value": round(us, 1), "unit": "us per step", "cores": 1, "kind": "reference",
+                                   "sample": f"{reps} decode steps of the reference CPU op (growing from 1024 "
+                                             "cached tokens), one thread"}
+    except Exception as exc:  # noqa: BLE001
+        out["cpu_baseline"] = {"unavailable": str(exc)[:200]}
+    return out
+
+
+def measure_config4(args):
+    """Config 4 (chunked prefill on the tensor cores) for the bench line:
+    causal-exact TFLOP/s over an 8192-token prompt in 512-token chunks."""
+    return prefill_numbers(argparse.Namespace(steps=3, warmup=2))
+
+
 # --------------------------------------------------------------------------
 def run_prefill(args):
+    line = prefill_numbers(args)
+    print(json.dumps(line), flush=True)
+
+
+def prefill_numbers(args):
     """Config 4: Qwen3-1.7B layer shape (Hq 16, Hkv 8, D 128), an 8192-token
     prompt in 512-token chunks; each chunk appended into pages and attended
     causally over all prior pages by the tensor-core kernel. A step = the
@@ -310,7 +403,7 @@ def run_prefill(args):
                          "kernel": "prefill_tc_kernel (+ kv_append_kernel), last chunk (8192 visible keys)",
                          "chunk_ms": [round(x, 4) for x in chunk_ms]},
             "clocks": clk}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_flash(args):
@@ -1116,6 +1209,16 @@ def main():
         "clocks": clk,
         "parity": parity,
     }
+    if rank == 0 and world == 1 and not args.no_other_configs:
+        # The other single-GPU configs, measured in the same run (not the
+        # headline): config 1 (0.6B layer decode) and config 4 (chunked
+        # prefill on the tensor cores).
+        c4 = measure_config4(args)
+        line["other_configs"] = {
+            "config1": measure_config1(args),
+            "config4": {"workload": c4["config"]["workload"], "tflops": c4["value"], "ms_per_prompt": c4["ms_per_step"],
+                        "last_chunk_tflops": c4["roofline"]["achieved"], "peak": c4["roofline"]["peak"],
+                        "frac_of_peak": round(c4["value"] / c4["roofline"]["peak"], 4)}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_step(args)  # warm-up (and set-up) step, untimed
         runs = [cpu_step(args) for _ in range(3)]
