@@ -81,6 +81,7 @@ struct DecodeParams {
     int32_t out_dtype;
     uint32_t* done_post;  // non-null (with merge): the last merger stores done_seq here
     uint32_t done_seq;
+    uint32_t* arrive;     // non-null (combine kernel merges): count of CTAs whose partials are written
     int32_t late_trigger;  // 1: release the next launch only after this grid's wait for its predecessor
     int32_t l2_prefetch_stages;  // stages past the ring brought into L2 while the ring is full
     int32_t n_kv_heads;
@@ -791,6 +792,15 @@ __global__ void __launch_bounds__(kThreads, 2)  // 96 registers: a combine CTA f
                 }
             }
         }
+    } else if (a.arrive != nullptr) {
+        // The combine waits for this count rather than for the grid to
+        // complete (GKV_DECODE_COMBINE_WAIT=count). The CTA's partials,
+        // appended row and table entries are ordered before it.
+        const int n_splits = a.step ? __ldg(&a.step->n_splits) : (int)gridDim.x;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0 && split < n_splits) atomicAdd(a.arrive, 1u);
+        PROBE_T(3);
     } else {
         __syncthreads();
         PROBE_T(3);
@@ -816,6 +826,8 @@ struct CombineParams {
     int32_t early;           // 1: the next launch is another layer's decode: trigger it at entry
     uint32_t* done;          // non-null: post done_seq here once the decode grid completed; trigger at entry
     uint32_t done_seq;
+    uint32_t* arrive;        // non-null: [0] decode CTAs arrived (wait for n_splits of them instead of the
+                             // grid's completion), [1] combine CTAs done (the last one resets both)
 #ifdef GKV_PROBE_TIMELINE
     int32_t probe_slot;
 #endif
@@ -846,11 +858,31 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     const bool gather = c.g.world > 1;
     const bool early = c.done != nullptr || (c.early && !gather);
     if (early) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
+    const int n_splits = c.step ? __ldg(&c.step->n_splits) : c.n_splits;
+    if (c.arrive != nullptr) {
+        // Wait (bounded) until every decode CTA has written its partials;
+        // one thread polls, the others wait at the barrier.
+        if (threadIdx.x == 0) {
+            const uint64_t t0 = global_timer_ns();
+            uint32_t v;
+            for (uint32_t i = 0;; ++i) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c.arrive) : "memory");
+                if (v >= (uint32_t)n_splits) break;
+                if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(c.err, kErrTimeout);
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are visible
+    }
     PROBE_C(1);
-    // The decode grid has completed: its pool rows and table entries are
-    // visible. Publish that for the next decode step of this table.
-    if (c.done != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    // Every decode CTA's pool rows and table entries are visible. Publish
+    // that for the next decode step of this table (with an arrival count,
+    // the last combine CTA does it once it has reset the count).
+    if (c.arrive == nullptr && c.done != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(c.done), "r"(c.done_seq) : "memory");
     // Otherwise only now may the next launch start: a decode step of the
     // same layer reads pages and table entries this step's decode grid
@@ -866,7 +898,6 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     __shared__ float s_l[kCombineWarps], s_a[kCombineWarps][kCombineDims], s_m[kCombineWarps];
     // One pass with an online rescale: each batch's loads are issued together.
     float M = -INFINITY, L = 0.f, A = 0.f;
-    const int n_splits = c.step ? __ldg(&c.step->n_splits) : c.n_splits;
     for (int b = 0; b * kBatch * kCombineWarps < n_splits; ++b) {
         float2 ml[kBatch];
         float av[kBatch];
@@ -907,6 +938,16 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     }
     s_a[w][lane] = A;
     __syncthreads();
+    if (c.arrive != nullptr && threadIdx.x == 0) {
+        // The last combine CTA to get here resets the counts for the next
+        // step of this table, then publishes the step's completion.
+        if (atomicAdd(c.arrive + 1, 1u) == gridDim.x * gridDim.y - 1u) {
+            c.arrive[0] = 0u;
+            c.arrive[1] = 0u;
+            if (c.done != nullptr)
+                asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(c.done), "r"(c.done_seq) : "memory");
+        }
+    }
     if (w == 0) {
         float Mt = -INFINITY;
 #pragma unroll
@@ -993,6 +1034,18 @@ int l2_prefetch_stages() {
     return n;
 }
 
+// GKV_DECODE_COMBINE_WAIT=count: the combine waits for the decode CTAs'
+// arrival count instead of the decode grid's completion. Off by default:
+// measured at 32k, the polling costs more (29.4 vs 28.0 us per layer) than
+// the earlier start saves.
+bool counted_combine() {
+    static const bool on = [] {
+        const char* v = getenv("GKV_DECODE_COMBINE_WAIT");
+        return v && v[0] == 'c';
+    }();
+    return on;
+}
+
 // GKV_DECODE_BOX=head selects the per-(page, head) boxes; the default is one
 // box per page and 64-dim half.
 bool page_boxes() {
@@ -1066,6 +1119,7 @@ cudaError_t launch_decode(const PoolView& pool, const DecodeMaps& maps, int2* ta
     p.done = d.post_done ? scratch.done : nullptr;
     p.done_expect = d.done_seq - 1u;
     p.merge = nullptr;
+    p.arrive = nullptr;
     p.out = d.out;
     p.out_dtype = d.out_dtype;
     p.done_post = nullptr;
@@ -1101,6 +1155,7 @@ cudaError_t launch_decode(const PoolView& pool, const DecodeMaps& maps, int2* ta
     // kernel.
     const bool fused = d.fused_merge && scratch.merge != nullptr && !(gather && gather->world > 1);
     p.late_trigger = 0;
+    p.arrive = (!fused && scratch.merge != nullptr && counted_combine()) ? scratch.merge : nullptr;
     if (fused) {
         p.merge = scratch.merge;
         p.done_post = d.post_done ? scratch.done : nullptr;
@@ -1143,6 +1198,7 @@ cudaError_t launch_decode(const PoolView& pool, const DecodeMaps& maps, int2* ta
     c.early = d.next_is_other_layer ? 1 : 0;
     c.done = d.post_done ? scratch.done : nullptr;
     c.done_seq = d.done_seq;
+    c.arrive = p.arrive;
 #ifdef GKV_PROBE_TIMELINE
     c.probe_slot = p.probe_slot;
 #endif

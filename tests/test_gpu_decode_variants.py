@@ -1,7 +1,8 @@
 """The decode kernel's build-time-equal, run-time-selected variants against
 the oracle: split merge inside the decode grid (GKV_DECODE_FUSED_MERGE=1),
-per-(page, head) TMA boxes (GKV_DECODE_BOX=head) and L2 prefetch of the
-stages past the ring (GKV_DECODE_L2_PREFETCH). The library reads these once
+per-(page, head) TMA boxes (GKV_DECODE_BOX=head), L2 prefetch of the
+stages past the ring (GKV_DECODE_L2_PREFETCH) and a combine that waits for
+the decode CTAs' arrival count (GKV_DECODE_COMBINE_WAIT=count). The library reads these once
 per process, so each variant runs in a child process: config 1 (Qwen3-0.6B
 layer), a 3-page context with a group of 8, 4 kv heads (2 pages per stage),
 and two consecutive steps across a page boundary, each checked against the
@@ -59,8 +60,9 @@ print("VARIANT OK")
 
 @pytest.mark.parametrize("env", [{"GKV_DECODE_FUSED_MERGE": "1"}, {"GKV_DECODE_BOX": "head"},
                                  {"GKV_DECODE_L2_PREFETCH": "4"},
-                                 {"GKV_DECODE_FUSED_MERGE": "1", "GKV_DECODE_L2_PREFETCH": "2"}],
-                         ids=["fused-merge", "head-boxes", "l2-prefetch", "fused+prefetch"])
+                                 {"GKV_DECODE_FUSED_MERGE": "1", "GKV_DECODE_L2_PREFETCH": "2"},
+                                 {"GKV_DECODE_COMBINE_WAIT": "count"}],
+                         ids=["fused-merge", "head-boxes", "l2-prefetch", "fused+prefetch", "counted-combine"])
 def test_decode_variant_matches_oracle(env):
     code = CHILD.replace("ROOT", repr(ROOT)).replace("HERE", repr(HERE))
     r = subprocess.run([sys.executable, "-c", code], env={**os.environ, **env}, capture_output=True, text=True,
