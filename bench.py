@@ -1,19 +1,25 @@
-"""Benchmark of the paged KV-cache decode path: Qwen3-4B layer-shape decode at 32k context (one GPU), and the same KV-head sharded over N GPUs.
+"""Benchmark of the paged KV-cache decode path: Qwen3-4B layer-shape decode
+at 32k context on one GPU, and the same KV-head sharded over N GPUs.
 
 Workload: Qwen3-4B layer shape (Hq=32, Hkv=8, D=128, bf16), 36 layers, each
 with 32768 cached tokens in a fragmented block table over a 4096-page pool
 (seeded permutation; synthetic N(0,1) values — the reference has no dataset).
-A step is one decode token through all 36 layers: per layer one fused launch
-that appends the token's K/V into its page and attends over the 32k+ tokens
-(split-K flash-decoding + split combine). The KV data of a step (36 x 128 MiB)
-is far larger than L2 (126 MB), so no L2 flush is needed between steps.
+A step is one decode token through all 36 layers: per layer one call of the
+public API, whose fused launch appends the token's K/V into its page and
+attends over the 32k+ tokens (split-K flash-decoding), then the split
+combine. Before timing, layer 0's output is checked against a torch fp32
+recomputation (`parity` in the line). The one-GPU default run also measures
+the 0.6B-layer decode (config 1) and the chunked prefill (config 4) under
+`other_configs`. The KV data of a step (36 x 128 MiB) is far larger than L2
+(126 MB), so no L2 flush is needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 N>1 (launched by torch.distributed.run, one rank per GPU): the 8 KV heads are
 sharded over the ranks (8/N each, the matching query heads with them), block
 tables are identical on every rank, and each layer's outputs are all-gathered
-with NCCL. Total work is fixed as N grows (strong scaling).
+inside the split combine over NVLink (--gather p2p, the default) or with NCCL
+(--gather nccl). Total work is fixed as N grows (strong scaling).
 
 --impl reference times the reference's own CPU op (oracle/_ref, compiled from
 the Genllm sources; else the C restatement) on the host cores on the same
