@@ -982,6 +982,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
         s_last = atomicAdd(c.g.ticket, 1u) == n_ctas - 1;
     }
     __syncthreads();
+    PROBE_C(3);
     if (!s_last) {
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         return;
@@ -996,6 +997,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
             asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(c.g.flag_dst[r]), "r"(c.g.epoch) : "memory");
     }
     __syncthreads();
+    PROBE_C(4);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Wait (bounded) until every peer's block for this layer and step arrived.
     if (threadIdx.x < c.g.world) {
@@ -1011,6 +1013,10 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
             }
         }
     }
+#ifdef GKV_PROBE_TIMELINE
+    __syncthreads();
+    PROBE_C(5);
+#endif
 }
 
 // GKV_NO_PDL=1 turns programmatic dependent launch off (plain stream order).
