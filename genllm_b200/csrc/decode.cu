@@ -993,7 +993,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
         // a release of every block this rank stored. A release store per
         // flag would put a system-scope fence in front of each of them.
         __threadfence_system();
-        for (int r = 0; r < c.g.world; ++r)
+        for (int r = 0; r < c.g.n_flag_dst; ++r)
             asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(c.g.flag_dst[r]), "r"(c.g.epoch) : "memory");
     }
     __syncthreads();
@@ -1001,7 +1001,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32, 3) paged_decode_combine_ke
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Wait (bounded) until every peer's block for this layer and step arrived.
     if (threadIdx.x < c.g.world) {
-        const uint32_t* f = c.g.flag_wait + threadIdx.x;
+        const uint32_t* f = c.g.flag_wait[threadIdx.x];
         const uint64_t t0 = global_timer_ns();
         uint32_t v;
         for (uint32_t i = 0;; ++i) {

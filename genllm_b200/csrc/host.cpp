@@ -1562,6 +1562,16 @@ struct gkv_gather {
     uint64_t wait_ns = 1000ull * 1000ull * 1000ull;  // limit of the wait for the peers' flags (1 s)
 };
 
+namespace {
+bool gather_flags_pulled() {
+    static const bool on = [] {
+        const char* v = getenv("GKV_GATHER_FLAGS");
+        return v && v[0] == 'p';
+    }();
+    return on;
+}
+}  // namespace
+
 extern "C" {
 
 int gkv_device_alloc(int device, size_t bytes, void** ptr) {
@@ -1665,11 +1675,19 @@ int gkv_paged_attention_gather(gkv_manager* m, int32_t layer_id, const void* Q, 
     gkv::GatherLaunch gl{};
     gl.world = gg->world;
     gl.rank = gg->rank;
+    // Flags pushed (default): this rank stores its flag into every rank's
+    // array and polls its own. Pulled (GKV_GATHER_FLAGS=pull): it stores only
+    // into its own array and polls the peers' over NVLink, so that the
+    // combine issues no remote store after its fence.
+    const bool pull = gather_flags_pulled();
+    gl.n_flag_dst = pull ? 1 : gg->world;
     for (int r = 0; r < gg->world; ++r) {
         gl.dst[r] = static_cast<char*>(gg->bases[r]) + out_offset + (size_t)gg->rank * block;
-        gl.flag_dst[r] = gg->flags[r] + (size_t)layer_id * gg->world + gg->rank;
+        if (!pull) gl.flag_dst[r] = gg->flags[r] + (size_t)layer_id * gg->world + gg->rank;
+        gl.flag_wait[r] = pull ? gg->flags[r] + (size_t)layer_id * gg->world + r
+                               : gg->flags[gg->rank] + (size_t)layer_id * gg->world + r;
     }
-    gl.flag_wait = gg->flags[gg->rank] + (size_t)layer_id * gg->world;
+    if (pull) gl.flag_dst[0] = gg->flags[gg->rank] + (size_t)layer_id * gg->world + gg->rank;
     gl.epoch = gg->epochs[layer_id] + 1;
     gl.ticket = gg->tickets + layer_id;
     gl.wait_ns = gg->wait_ns;

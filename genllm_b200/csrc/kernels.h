@@ -120,8 +120,9 @@ struct GatherLaunch {
     int32_t world;                        // 0 = no gather
     int32_t rank;
     void* dst[kMaxGatherRanks];           // this rank's head block in rank r's full buffer
-    uint32_t* flag_dst[kMaxGatherRanks];  // this rank's flag slot (this layer) on rank r
-    const uint32_t* flag_wait;            // this layer's slots on this rank, world entries
+    int32_t n_flag_dst;                   // flag slots this rank publishes to (world, or 1)
+    uint32_t* flag_dst[kMaxGatherRanks];  // this rank's flag slot (this layer): on every rank, or its own
+    const uint32_t* flag_wait[kMaxGatherRanks];  // where rank r's flag for this layer is read
     uint32_t epoch;                       // call count of this layer, 1-based
     uint32_t* ticket;                     // CTA completion counter (zero between launches)
     uint64_t wait_ns;                     // limit of the wait for the peers' flags
