@@ -47,11 +47,22 @@ constexpr uint32_t kOffK = kOffQ + kTile;
 constexpr uint32_t kOffV = kOffK + kStages * kTile;
 constexpr uint32_t kOffBar = kOffV + kStages * kTile;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, TMEM slot, alignment slack
-static_assert((6 + 4 * kStages) * 8 + 4 <= 256, "barriers and the TMEM slot fit their 256 bytes");
-// TMEM columns: S/P of two tiles [0, 256), O [256, 384), Q as the A operand
-// of Q K^T [384, 448) (bf16 pairs), max/sum exchange [448, 452).
+static_assert((9 + 4 * kStages) * 8 + 4 <= 256, "barriers and the TMEM slot fit their 256 bytes");
+// (m, l) rows of the two softmax groups at the end: the last 4 KiB of the
+// last V stage.
+constexpr uint32_t kOffEx = kOffV + kStages * kTile - 4096;
+// Cluster merge: a sender's partials (O rows [128][128] fp32, then (m, l)
+// per row), one receive slot per other CTA of the cluster (up to 2) from
+// offset 0 of the leader; the output tile is staged after them.
+constexpr uint32_t kRecvO = 128 * kHeadDim * 4;
+constexpr uint32_t kRecvSlot = kRecvO + 128 * 8;
+constexpr uint32_t kOffStage = (2 * kRecvSlot + 1023) / 1024 * 1024;
+static_assert(kOffStage + 128 * kHeadDim * 4 <= kOffEx, "staged output tile clear of the (m, l) exchange");
+static_assert(kRecvSlot % 16 == 0, "bulk copy size and slot offsets are multiples of 16 bytes");
+// TMEM columns: S/P of the two groups' tiles [0, 256) (buffer = tile & 1 =
+// group), O of group 0 [256, 384), O of group 1 [384, 512).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256, kColQ = 384, kColX = 448;
+constexpr uint32_t kColO = 256;
 
 struct TcParams {
     const int2* table;
@@ -70,7 +81,7 @@ struct TcParams {
     float qscale;    // softmax scale * log2(e)
 };
 
-constexpr int kConsumerThreads = 256;               // 8 warps: 2 threads per query row
+constexpr int kConsumerThreads = 256;               // 8 warps: two groups of one thread per query row
 constexpr int kLoadWarp = kConsumerThreads / 32;   // issues the K loads (warp + 1: the V loads)
 constexpr int kMmaWarp = kLoadWarp + 2;            // issues the tcgen05 MMAs
 constexpr int kThreadsTc = kConsumerThreads + 96;
@@ -82,11 +93,14 @@ constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
 __device__ long long g_probe_pf[2 * 128 * 16];
 __device__ long long g_probe_mma[128 * 4];
 __device__ long long g_probe_ld[128 * 8];
-__device__ unsigned long long g_probe_ee[1024 * 4];  // per CTA: entry, setup done, first S ready, exit
+// Per CTA: entry, setup done, first S ready, exit, every MMA done, groups
+// merged, cluster merged, output stored, first cluster barrier passed,
+// DSMEM sends issued, second cluster barrier passed.
+__device__ unsigned long long g_probe_ee[1024 * 16];
 #define PROBE_EE(k)                                                                                          \
     if (tid == 0) {                                                                                          \
         const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;                      \
-        if (cta < 1024) g_probe_ee[cta * 4 + (k)] = global_timer_ns();                                      \
+        if (cta < 1024) g_probe_ee[cta * 16 + (k)] = global_timer_ns();                                      \
     }
 #define PROBE_LD(k)                                                                                  \
     if (blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 1 && j < 128) g_probe_ld[j * 8 + (k)] = clock64();
@@ -139,6 +153,26 @@ __device__ __forceinline__ int tile_key(int c, int mode) {
     return mode == 2 ? (((kPagesPerTile - 1 - (c >> 4)) << 4) | (c & 15)) : c;
 }
 
+// Output conversion of the epilogue: two fp32 values -> packed bf16 (lo in
+// the low half) by the hardware's round-to-nearest-even. For normal values
+// these are the reference's bits (include/utils/bfloat16.hpp:18-41 rounds to
+// nearest even); it differs only where the reference flushes a zero-exponent
+// input to a signed zero (a difference below 2^-126) and in the payload of a
+// NaN. Anything longer costs here: the epilogue runs once per CTA from a
+// cold instruction cache, and its time grew with the code size (a per-value
+// special-case check took ~1 us more per tile).
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+__device__ __noinline__ uint4 half8_rn(float4 x, float4 y) {
+    auto h2 = [](float u, float v) {
+        return (uint32_t)__half_as_ushort(__float2half_rn(u)) | ((uint32_t)__half_as_ushort(__float2half_rn(v)) << 16);
+    };
+    return make_uint4(h2(x.x, x.y), h2(x.z, x.w), h2(y.x, y.y), h2(y.z, y.w));
+}
+
 __global__ void __launch_bounds__(kThreadsTc, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                       const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap k_run,
@@ -150,11 +184,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     uint64_t* bar_v = bar_k + kStages;       // [kStages] V tile landed
     uint64_t* bar_kfree = bar_v + kStages;   // [kStages] Q K^T of the stage's tile done
     uint64_t* bar_vfree = bar_kfree + kStages;  // [kStages] P V of the stage's tile done
-    uint64_t* bar_s = bar_vfree + kStages;   // [2] S of a tile in its TMEM buffer
-    uint64_t* bar_o = bar_s + 2;             // P V of a tile done (in issue order)
-    uint64_t* bar_p = bar_o + 1;             // consumers: P of a tile written (and S of it read)
-    uint64_t* bar_qt = bar_p + 1;            // consumers: Q copied into TMEM
-    constexpr int kNumBars = 6 + 4 * kStages;  // q, k, v, kfree, vfree, s[2], o, p, qt
+    uint64_t* bar_s = bar_vfree + kStages;   // [2] S of a tile in its TMEM buffer (buffer = tile & 1)
+    uint64_t* bar_o = bar_s + 2;             // [2] P V into O of a group done
+    uint64_t* bar_p = bar_o + 2;             // [2] a group's 4 warps: P of its tile written (S read)
+    uint64_t* bar_fin = bar_p + 2;           // every MMA of the CTA done
+    uint64_t* bar_recv = bar_fin + 1;        // cluster leader: the other CTAs' partials landed
+    constexpr int kNumBars = 9 + 4 * kStages;  // q, k, v, kfree, vfree, s[2], o[2], p[2], fin, recv
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + kNumBars);
 
     const int tid = threadIdx.x;
@@ -184,6 +219,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
     if (tid == 0) {
         for (int b = 0; b < kNumBars; ++b) mbar_init(bar_q + b, 1);
+        mbar_init(&bar_p[0], 4);
+        mbar_init(&bar_p[1], 4);
         fence_mbar_init();
     }
     tc::fence_before_sync();
@@ -192,8 +229,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     PROBE_EE(1);
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
-    const uint32_t t_o = tmem + lane_base + kColO;           // this warp's lanes of O
 
+    const uint32_t sQ = smem_addr(smem + kOffQ);
     const uint32_t sK = smem_addr(smem + kOffK);
     const uint32_t sV = smem_addr(smem + kOffV);
     // Q is read once; K and V tiles are read again by the CTAs of the other
@@ -262,93 +299,102 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, false, true);
 
     bool ok = true;
-    // The consumer warps' own barrier (the load warp never joins it).
+    // The consumer warps' own barrier (the load and MMA warps never join it).
     auto consumer_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); };
     // A wait that times out clears `ok`; later waits are then skipped, but
     // every thread still reaches every __syncthreads, so nothing can hang.
     auto wait = [&](uint64_t* bar, uint32_t parity) {
         if (ok && !mbar_wait_bounded(bar, parity)) ok = false;
     };
-    // S(j) = Q K(j)^T into TMEM columns [(j & 1) * 128, +128), Q read from
-    // TMEM: only K streams from shared memory, whose bandwidth bounds an
-    // N = 128 MMA with both operands there.
     // The MMA warp runs converged; one elected lane issues. Descriptors are
     // built once and stepped by adding the byte offset / 16 to their address
     // field (smem addresses stay below 256 KiB, so the 14-bit field cannot
     // carry). A tight issue sequence keeps the tensor pipe fed: each
     // m128n128k16 MMA takes 64 cycles, about what loose issue code spends
     // between two MMAs.
+    const uint64_t desc_q0 = tc::smem_desc_sw128(sQ, 16, 1024);
     const uint64_t desc_k0 = tc::smem_desc_sw128(sK, 16, 1024);
     const uint64_t desc_v0 = tc::smem_desc_sw128(sV, kHalf, 1024);
+    // S(j) = Q K(j)^T into TMEM columns [(j & 1) * 128, +128), both operands
+    // from shared memory (K-major, 128-byte swizzle).
     auto issue_qk = [&](int j) {
         const int sb = j & 1, st = j % kStages;
         wait(&bar_k[st], (j / kStages) & 1);
-        PROBE_LD(6);
+        PROBE_MMA(3);
         tc::fence_after_sync();
         if (tc::elect_one()) {
             const uint64_t dk = desc_k0 + ((st * kTile) >> 4);
             const uint32_t d = tmem + sb * 128;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-                tc::mma_bf16_ts(d, tmem + kColQ + kk * 8, dk + ((((kk >> 2) * kHalf) + (kk & 3) * 32) >> 4), kIdescQK,
-                                kk > 0);
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (((kk >> 2) * kHalf) + (kk & 3) * 32) >> 4;
+                tc::mma_bf16(d, desc_q0 + off, dk + off, kIdescQK, kk > 0);
+            }
             tc::commit(&bar_s[sb]);
             tc::commit(&bar_kfree[st]);
         }
         __syncwarp();
     };
 
-    // P(j) V(j) into the O columns [256, 384), both bf16 terms of P, with P
-    // read from TMEM (where it replaced S(j)).
+    // P(j) V(j) into the O columns of group j & 1, both bf16 terms of P, with
+    // P read from TMEM (where it replaced S(j)).
     auto issue_pv = [&](int j) {
-        const int sb = j & 1, st = j % kStages;
+        const int g = j & 1, st = j % kStages;
+        wait(&bar_v[st], (j / kStages) & 1);
+        tc::fence_after_sync();
         if (tc::elect_one()) {
             const uint64_t dv = desc_v0 + ((st * kTile) >> 4);
-            const uint32_t p = tmem + sb * 128;
+            const uint32_t p = tmem + g * 128;
+            const uint32_t o = tmem + kColO + g * 128;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
-                tc::mma_bf16_ts(tmem + kColO, p + kk * 8, dv + ((kk * 2048) >> 4), kIdescPV, j > 0 || kk > 0);
-                tc::mma_bf16_ts(tmem + kColO, p + 64 + kk * 8, dv + ((kk * 2048) >> 4), kIdescPV, true);
+                tc::mma_bf16_ts(o, p + kk * 8, dv + ((kk * 2048) >> 4), kIdescPV, j >= 2 || kk > 0);
+                tc::mma_bf16_ts(o, p + 64 + kk * 8, dv + ((kk * 2048) >> 4), kIdescPV, true);
             }
-            tc::commit(bar_o);
+            tc::commit(&bar_o[g]);
             tc::commit(&bar_vfree[st]);
         }
         __syncwarp();
     };
 
-    // Warp-specialised software pipeline. The consumer warps (0-7) run the
-    // softmax of tile j while the tensor cores compute S of tile j+1 (two S
-    // buffers in TMEM). One load warp issues K(j) once QK(j-3) has freed its
-    // stage, another V(j) once PV(j-3) has; the MMA warp
-    // issues QK(0), QK(1), then per tile PV(j) once the consumers have written
-    // P(j), followed by QK(j+2) into the TMEM buffer P(j) occupied.
+    // Warp-specialised software pipeline with two softmax groups. The KV
+    // tiles of the CTA alternate between group 0 (warps 0-3, even tiles) and
+    // group 1 (warps 4-7, odd tiles); each group keeps its own running max,
+    // sum and O accumulator for all 128 query rows (one thread per row), so
+    // one group's softmax runs while the tensor cores compute the other
+    // group's P V and next Q K^T. The groups' (m, l, O) are merged at the end.
+    // One load warp issues K(j) once QK(j-3) has freed its stage, another V(j)
+    // once PV(j-3) has; the MMA warp issues QK(0), QK(1), then per tile PV(j)
+    // once group j & 1 has written P(j), followed by QK(j+2) into the TMEM
+    // buffer P(j) occupied once PV(j) is done.
     if (warp == kMmaWarp) {
         if (n_tiles > 0) {
-            wait(bar_qt, 0);
+            wait(bar_q, 0);
             tc::fence_after_sync();
             issue_qk(0);
             if (n_tiles > 1) issue_qk(1);
             for (int j = 0; j < n_tiles && ok; ++j) {
-                wait(bar_p, j & 1);
+                wait(&bar_p[j & 1], (j >> 1) & 1);
                 PROBE_MMA(0);
                 tc::fence_after_sync();
                 if (!ok) break;
                 issue_pv(j);
                 if (j + 2 < n_tiles) {
-                    wait(bar_o, j & 1);  // QK(j+2) overwrites P(j) in TMEM
+                    wait(&bar_o[j & 1], (j >> 1) & 1);  // QK(j+2) overwrites P(j) in TMEM
                     PROBE_MMA(1);
                     tc::fence_after_sync();
                     issue_qk(j + 2);
                     PROBE_MMA(2);
                 }
             }
+            // Tracks every MMA this thread issued: both groups' O are final.
+            if (tc::elect_one()) tc::commit(bar_fin);
+            __syncwarp();
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
-        if (n_split > 1) {  // the consumers' two cluster barriers
+        if (n_split > 1)  // the consumers' cluster barrier (every CTA's MMAs done)
             asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-            asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-        }
         tc::fence_before_sync();
         __syncthreads();
         return;
@@ -380,42 +426,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
-        if (n_split > 1) {  // the consumers' two cluster barriers
+        if (n_split > 1)  // the consumers' cluster barrier (every CTA's MMAs done)
             asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-            asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-        }
         tc::fence_before_sync();
         __syncthreads();
         return;
     }
 
     const int r = tid & 127;  // query row of this thread
-    const int hc = tid >> 7;  // which 64 of the 128 key columns (and O columns)
-    const uint32_t t_x = tmem + lane_base + kColX;  // exchange columns: [kColX + 2 hc, +2)
-    if (n_tiles > 0) {
-        // Q into TMEM: this thread's row r, dims [64 hc, +64) from the
-        // swizzled smem tile, two dims per column (lower dim in the low half).
-        wait(bar_q, 0);
-        uint32_t qw[32];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint4 v = *reinterpret_cast<const uint4*>(smem + kOffQ + hc * kHalf + r * 128 + ((c ^ (r & 7)) << 4));
-            qw[4 * c] = v.x;
-            qw[4 * c + 1] = v.y;
-            qw[4 * c + 2] = v.z;
-            qw[4 * c + 3] = v.w;
-        }
-        tc::st32(tmem + lane_base + kColQ + hc * 32, *reinterpret_cast<const float(*)[32]>(qw));
-        tc::wait_st();
-        tc::fence_before_sync();
-        consumer_sync();
-        if (tid == 0) mbar_arrive(bar_qt);
-    }
+    const int g = tid >> 7;   // softmax group: KV tiles g, g + 2, ...
     const int q_abs = first_q_abs + r;
     const int lim = a.causal ? min(q_abs, a.total - 1) : a.total - 1;  // last visible key
     float m_run = -INFINITY, l_run = 0.f;
-    // Lanes 0-7 of every consumer warp hold the next tile's page entries
-    // (fetched a tile ahead) to derive its copy mode.
+    // Lanes 0-7 of every consumer warp hold the page entries of the group's
+    // next tile (fetched a tile ahead) to derive its copy mode.
     const int lane = tid & 31;
     auto entry = [&](int j) {
         if (a.contig) return make_int2(-1, -1);  // no table: every tile is in key order (mode 0)
@@ -423,59 +447,47 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         if (lp >= a.n_pages) lp = a.n_pages - 1;
         return a.table[lp];
     };
-    int2 next_e = n_tiles > 0 ? entry(0) : make_int2(0, 0);
+    int2 next_e = g < n_tiles ? entry(g) : make_int2(0, 0);
+    const uint32_t t_s = tmem + lane_base + g * 128;           // this group's S / P buffer, this warp's lanes
+    const uint32_t t_o = tmem + lane_base + kColO + g * 128;   // this group's O
 
-    // S(j) is loaded from TMEM at the end of tile j-1, so the load latency
-    // overlaps the loop turn-around.
-    float s[64];
-    auto load_s = [&](int j) {
-        wait(&bar_s[j & 1], (j >> 1) & 1);
-        if (j == 0) { PROBE_EE(2); }
-        tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-            tc::ld32(tmem + lane_base + (j & 1) * 128 + hc * 64 + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
-    };
-    if (n_tiles > 0) load_s(0);
-
-    for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
+    for (int j = g; j < n_tiles; j += 2) {
         const int2 cur_e = next_e;  // page entries of tile j (lanes 0-7)
-        if (j + 1 < n_tiles) next_e = entry(j + 1);
+        if (j + 2 < n_tiles) next_e = entry(j + 2);
         PROBE_PF(0);
         const int key0 = (j0 + j) * kBN;
+        // S(j) is ready; its commit also tracks P V of this group's previous
+        // tile (issued before QK(j)), so O may be rescaled without a wait.
+        wait(&bar_s[g], (j >> 1) & 1);
+        if (j == 0) { PROBE_EE(2); }
+        tc::fence_after_sync();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc::ld32(t_s + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
         tc::wait_ld_into(*reinterpret_cast<float(*)[32]>(&s[0]));
         tc::reg_dep(*reinterpret_cast<float(*)[32]>(&s[32]));
+        tc::reg_dep(*reinterpret_cast<float(*)[32]>(&s[64]));
+        tc::reg_dep(*reinterpret_cast<float(*)[32]>(&s[96]));
         PROBE_PF(1);
 
-        // Row max over the tile: local over this thread's 64 keys, then one
-        // exchange with the row's other thread through spare TMEM columns.
-        // Scores stay unscaled here (qscale > 0 keeps the order).
+        // Row max over the tile (scores unscaled: qscale > 0 keeps the order).
         const int n_ok = max(0, min(kBN, lim - key0 + 1));  // keys [0, n_ok) of the tile are visible
         if (!__all_sync(0xFFFFFFFFu, n_ok >= kBN)) {
             const int mode = tile_mode_warp(cur_e, lane, a.pool_pages, a.runs);
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-                if (tile_key(hc * 64 + c, mode) >= n_ok) s[c] = -INFINITY;
+            for (int c = 0; c < 128; ++c)
+                if (tile_key(c, mode) >= n_ok) s[c] = -INFINITY;
         }
-        float mx = s[0];
+        float mx4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-        for (int c = 1; c < 64; ++c) mx = fmaxf(mx, s[c]);
+        for (int c = 4; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         PROBE_PF(2);
-        tc::st2(t_x + 2 * hc, mx, 0.f);
-        tc::wait_st();
-        tc::fence_before_sync();
-        consumer_sync();
-        tc::fence_after_sync();
-        PROBE_PF(3);
-        float mx2, unused;
-        tc::ld2(t_x + 2 * (1 - hc), mx2, unused);
-        tc::wait_ld();
         // Lazy rescaling: the reference max m_run moves only when the tile's
         // max exceeds it by more than kRescaleLog2 (P then stays <= 2^8, exact
         // in the fp32 accumulators and the hi/lo split); O and l are rescaled
-        // only then, so most tiles never wait for the previous P V.
-        const float m_tile = fmaxf(mx, mx2) * a.qscale;
+        // only then.
+        const float m_tile = mx * a.qscale;
         const bool move = m_tile > m_run + kRescaleLog2;
         const float m_new = move ? m_tile : m_run;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
@@ -486,18 +498,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         // so hi + lo carries P to 2^-14, where a single bf16 P would lose 2^-9
         // per probability. Packed two keys per 32-bit word, lower key in the
         // low half, as the MMA reads A from TMEM. Four partial sums keep the
-        // dependent FADD chain short.
-        // Two passes of 32 keys; each pass's stores to TMEM run while the
-        // next pass computes.
+        // dependent FADD chain short. Four passes of 32 keys; each pass's
+        // stores to TMEM run while the next pass computes.
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
         const float neg_m = -m_use;
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
+        for (int c4 = 0; c4 < 4; ++c4) {
             uint32_t hw[16], lw[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                const float p0 = exp2_approx(fmaf(s[h2 * 32 + 2 * i], a.qscale, neg_m));
-                const float p1 = exp2_approx(fmaf(s[h2 * 32 + 2 * i + 1], a.qscale, neg_m));
+                const float p0 = exp2_approx(fmaf(s[c4 * 32 + 2 * i], a.qscale, neg_m));
+                const float p1 = exp2_approx(fmaf(s[c4 * 32 + 2 * i + 1], a.qscale, neg_m));
                 sum4[i & 3] += p0 + p1;
                 const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
                 hw[i] = __byte_perm(b0, b1, 0x7632);
@@ -505,123 +516,147 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 lw[i] = __byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632);
             }
             // P(j) overwrites S(j) in TMEM: hi in the buffer's columns
-            // [0, 64), lo in [64, 128); this thread's 64 keys are 32 columns
-            // of each.
-            tc::st16(tmem + lane_base + st * 128 + hc * 32 + h2 * 16, hw);
-            tc::st16(tmem + lane_base + st * 128 + 64 + hc * 32 + h2 * 16, lw);
+            // [0, 64), lo in [64, 128).
+            tc::st16(t_s + c4 * 16, hw);
+            tc::st16(t_s + 64 + c4 * 16, lw);
         }
         const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
         PROBE_PF(4);
-        l_run = l_run * alpha + sum;  // this thread's share of the row sum
+        l_run = l_run * alpha + sum;
         m_run = m_new;
 
-        if (j > 0 && __any_sync(0xFFFFFFFFu, move)) {
-            // P V of tile j-1 must be done before O is rescaled. (The stage's
-            // previous P V is done already: V(j-1) was loaded into the stage
-            // after it, so the barrier's parity identifies PV(j-1).)
-            wait(&bar_vfree[(j - 1) % kStages], ((j - 1) / kStages) & 1);
-            tc::fence_after_sync();
-            {
+        if (j >= 2 && __any_sync(0xFFFFFFFFu, move)) {
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                float o[32];
+                tc::ld32(t_o + c * 32, o);
+                tc::wait_ld();
 #pragma unroll
-                for (int c = hc * 2; c < hc * 2 + 2; ++c) {
-                    float o[32];
-                    tc::ld32(t_o + c * 32, o);
-                    tc::wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                    tc::st32(t_o + c * 32, o);
-                }
+                for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                tc::st32(t_o + c * 32, o);
             }
         }
         tc::wait_st();
         PROBE_PF(5);
-        // V(j) must have landed; zero its rows past the cache (P is 0 there,
-        // but stale rows could hold NaN or Inf).
-        const int vst = j % kStages;
-        wait(&bar_v[vst], (j / kStages) & 1);
-        PROBE_PF(6);
+        // Past the cache in the last tile: zero V's rows once it has landed
+        // (P is 0 there, but stale rows could hold NaN or Inf).
         const int valid_rows = min(kBN, a.total - key0);
         if (valid_rows < kBN) {  // CTA-uniform
+            const int vst = j % kStages;
+            wait(&bar_v[vst], (j / kStages) & 1);
             const int mode = tile_mode_warp(cur_e, lane, a.pool_pages, a.runs);
             if (tile_key(r, mode) >= valid_rows) {
-                uint4* v0 = reinterpret_cast<uint4*>(smem + kOffV + vst * kTile + hc * kHalf + r * 128);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) v0[c] = make_uint4(0, 0, 0, 0);
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint4* v0 = reinterpret_cast<uint4*>(smem + kOffV + vst * kTile + hf * kHalf + r * 128);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) v0[c] = make_uint4(0, 0, 0, 0);
+                }
             }
             fence_proxy_async_smem();
         }
         tc::fence_before_sync();
-        consumer_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_p[g]);
         PROBE_PF(7);
-        if (tid == 0) mbar_arrive(bar_p);
-        PROBE_PF(8);
-        if (j + 1 < n_tiles) load_s(j + 1);
     }
 
-    if (n_tiles > 0) wait(bar_o, (n_tiles - 1) & 1);
+    // Merge the two groups: thread (r, g) produces dims [64 g, +64) of row r
+    // from both groups' O columns and (m, l) rows exchanged through shared
+    // memory (the tail of the last V stage, idle once every MMA is done and
+    // clear of the cluster merge's receive area).
+    if (n_tiles > 0) wait(bar_fin, 0);
+    PROBE_EE(4);
     tc::fence_after_sync();
+    float2* ex = reinterpret_cast<float2*>(smem + kOffEx);
+    ex[g * 128 + r] = make_float2(m_run, l_run);
+    consumer_sync();
+    const float2 oth = ex[(1 - g) * 128 + r];
+    const float m0 = g == 0 ? m_run : oth.x, l0 = g == 0 ? l_run : oth.y;
+    const float m1 = g == 0 ? oth.x : m_run, l1 = g == 0 ? oth.y : l_run;
+    const float Mg = fmaxf(m0, m1);
+    const float Mgs = Mg == -INFINITY ? 0.f : Mg;
+    const float f0 = exp2_approx(m0 - Mgs), f1 = exp2_approx(m1 - Mgs);
+    const int hc = g;  // which 64 of the 128 output dims this thread owns
     float o[64];
 #pragma unroll
-    for (int c = 0; c < 2; ++c) tc::ld32(t_o + hc * 64 + c * 32, *reinterpret_cast<float(*)[32]>(&o[c * 32]));
-    tc::wait_ld();  // warp-collective: executed even on the error path
-    if (n_tiles == 0) {
+    for (int c = 0; c < 2; ++c) {
+        float a0[32], a1[32];
+        tc::ld32(tmem + lane_base + kColO + hc * 64 + c * 32, a0);
+        tc::ld32(tmem + lane_base + kColO + 128 + hc * 64 + c * 32, a1);
+        tc::wait_ld();  // warp-collective: executed even on the error path
 #pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = 0.f;
+        for (int i = 0; i < 32; ++i) {
+            // Group 1 has no tile when n_tiles < 2 (its O was never written);
+            // neither group has one when n_tiles == 0.
+            const float x0 = n_tiles > 0 ? a0[i] * f0 : 0.f;
+            o[c * 32 + i] = n_tiles > 1 ? fmaf(a1[i], f1, x0) : x0;
+        }
     }
-    {
-        // Each thread holds the sum over its own 64 keys of every tile.
-        tc::st2(t_x + 2 * hc, l_run, 0.f);
-        tc::wait_st();
-        tc::fence_before_sync();
-        consumer_sync();
-        tc::fence_after_sync();
-        float l2, unused;
-        tc::ld2(t_x + 2 * (1 - hc), l2, unused);
-        tc::wait_ld();
-        l_run += l2;
-    }
+    m_run = Mg;
+    l_run = (n_tiles > 0 ? l0 * f0 : 0.f) + (n_tiles > 1 ? l1 * f1 : 0.f);
     float l_fin = l_run;
+    PROBE_EE(5);
     if (n_split > 1) {
-        // Merge through distributed shared memory: the other CTAs of the
-        // cluster send (m, l, O row half) into the leader's (now idle) buffers.
-        tc::fence_before_sync();
-        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-        constexpr uint32_t kRecvO = 128 * kHeadDim * 4;  // 64 KiB per sending CTA
-        constexpr uint32_t kRecvMl = 3 * kRecvO;
+        // Merge through distributed shared memory. Each other CTA of the
+        // cluster writes its (O row, m, l) partials into its own (now idle)
+        // shared memory and sends them with ONE bulk copy into the leader's
+        // receive slot, completing on the leader's bar_recv: per-thread
+        // st.shared::cluster stores of the same 64 KiB ran at ~10 B/clk
+        // (~3 us), the bulk copy at the DSMEM link rate. Rows are 512 bytes
+        // apart, so the 16-byte pieces of a row are XOR-permuted by the
+        // row's low 3 bits: the 8 threads of one shared-memory phase
+        // (consecutive rows) then hit distinct banks.
         const uint32_t row_off = r * kHeadDim * 4 + hc * 64 * 4;
+        if (rank == 0 && tid == 0) mbar_arrive_expect_tx(bar_recv, (n_split - 1) * kRecvSlot);
         if (rank > 0) {
-            const uint32_t local = smem_addr(smem + (rank - 1) * kRecvO + row_off);
-            uint32_t remote;
-            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(local));
+            float4* mine = reinterpret_cast<float4*>(smem + row_off);
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-                asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote + i * 16), "f"(o[4 * i]),
-                             "f"(o[4 * i + 1]), "f"(o[4 * i + 2]), "f"(o[4 * i + 3])
-                             : "memory");
-            if (hc == 0) {
-                const uint32_t lml = smem_addr(smem + kRecvMl + ((rank - 1) * 128 + r) * 8);
-                uint32_t rml;
-                asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rml) : "r"(lml));
-                asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(rml), "f"(m_run), "f"(l_run) : "memory");
-            }
+                mine[i ^ (r & 7)] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            if (hc == 0) reinterpret_cast<float2*>(smem + kRecvO)[r] = make_float2(m_run, l_run);
+            fence_proxy_async_smem();
         }
+        // Every CTA's MMAs are done (its shared memory may be overwritten) and
+        // the senders' partials are written.
+        tc::fence_before_sync();
         asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        PROBE_EE(8);
+        if (rank > 0 && tid == 0) {
+            uint32_t dst, bar;
+            const uint32_t ldst = smem_addr(smem + (rank - 1) * kRecvSlot);
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(dst) : "r"(ldst));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(bar) : "r"(smem_addr(bar_recv)));
+            asm volatile(
+                "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n\t"
+                "cp.async.bulk.commit_group;" ::"r"(dst),
+                "r"(smem_addr(smem)), "r"(kRecvSlot), "r"(bar)
+                : "memory");
+            PROBE_EE(9);
+            // The source must stay valid until the copy has read it.
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        }
+        // Waited for even after an earlier timeout: the leader must not exit
+        // while copies into its shared memory are in flight.
+        if (rank == 0 && !mbar_wait_bounded(bar_recv, 0)) ok = false;
+        PROBE_EE(10);
         if (rank == 0) {
             float M = m_run;
-            for (int k = 1; k < n_split; ++k) M = fmaxf(M, reinterpret_cast<const float2*>(smem + kRecvMl)[(k - 1) * 128 + r].x);
+            for (int k = 1; k < n_split; ++k)
+                M = fmaxf(M, reinterpret_cast<const float2*>(smem + (k - 1) * kRecvSlot + kRecvO)[r].x);
             const float Ms = M == -INFINITY ? 0.f : M;
             const float f0 = exp2_approx(m_run - Ms);
             l_fin = l_run * f0;
 #pragma unroll
             for (int i = 0; i < 64; ++i) o[i] *= f0;
             for (int k = 1; k < n_split; ++k) {
-                const float2 ml = reinterpret_cast<const float2*>(smem + kRecvMl)[(k - 1) * 128 + r];
+                const float2 ml = reinterpret_cast<const float2*>(smem + (k - 1) * kRecvSlot + kRecvO)[r];
                 const float f = exp2_approx(ml.x - Ms);
                 l_fin = fmaf(ml.y, f, l_fin);
-                const float4* src = reinterpret_cast<const float4*>(smem + (k - 1) * kRecvO + row_off);
+                const float4* src = reinterpret_cast<const float4*>(smem + (k - 1) * kRecvSlot + row_off);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float4 v = src[i];
+                    const float4 v = src[i ^ (r & 7)];
                     o[4 * i] = fmaf(v.x, f, o[4 * i]);
                     o[4 * i + 1] = fmaf(v.y, f, o[4 * i + 1]);
                     o[4 * i + 2] = fmaf(v.z, f, o[4 * i + 2]);
@@ -630,50 +665,59 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
         }
     }
+#ifdef GKV_PROBE_TIMELINE
+#pragma unroll
+    for (int i = 0; i < 64; ++i) asm volatile("" ::"f"(o[i]));
+#endif
+    PROBE_EE(6);
     const float inv = 1.f / l_fin;
-    // Output tile [128 queries][128 dims] through shared memory (the V stage
-    // buffers, idle now and clear of the merge's receive area), then stored
-    // with consecutive threads on consecutive 16-byte pieces of a row: each
-    // thread alone holds 64 elements of one row, and rows are 256 or 512
-    // bytes apart, so direct stores would touch a new line per lane.
+#ifdef GKV_PROBE_TIMELINE
+    asm volatile("" ::"f"(inv));
+    PROBE_EE(13);
+#endif
+    // Output tile [128 queries][128 dims] through shared memory (idle stage
+    // buffers clear of the merge's receive slots): each thread alone holds
+    // 64 elements of one row, and rows are 256 or 512 bytes apart, so direct
+    // stores would touch a new line per lane. The normalised fp32 rows are
+    // staged first (16-byte pieces XOR-permuted by the row's low 3 bits:
+    // bank-conflict free on both sides, as in the merge); then a compact loop
+    // converts to the output dtype with consecutive threads on consecutive
+    // 16-byte pieces of the output. This code runs once per CTA from a cold
+    // instruction cache, so it is kept short: a fully unrolled conversion of
+    // the 64 register values cost ~2 us per CTA, and time grew with the code
+    // size of the conversion rather than with its instruction count.
     if (rank == 0) {
-        const int es = a.out_dtype == 0 ? 4 : 2;
-        uint8_t* stile = smem + kOffV;
-        uint8_t* mine = stile + r * kHeadDim * es + hc * 64 * es;
-        if (es == 4) {
+        uint8_t* stile = smem + kOffStage;
+        float4* mine = reinterpret_cast<float4*>(stile + r * kHeadDim * 4 + hc * 64 * 4);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                reinterpret_cast<float4*>(mine)[i] =
-                    make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t w[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float v0 = o[8 * i + 2 * k] * inv, v1 = o[8 * i + 2 * k + 1] * inv;
-                    uint32_t b0, b1;
-                    if (a.out_dtype == 30) {
-                        b0 = bf16_bits_ref(v0);
-                        b1 = bf16_bits_ref(v1);
-                    } else {
-                        b0 = __half_as_ushort(__float2half_rn(v0));
-                        b1 = __half_as_ushort(__float2half_rn(v1));
-                    }
-                    w[k] = b0 | (b1 << 16);
-                }
-                reinterpret_cast<uint4*>(mine)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int i = 0; i < 16; ++i)
+            mine[i ^ (r & 7)] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+        PROBE_EE(11);
+        consumer_sync();
+        PROBE_EE(12);
+        const int rows = min(kBM, S - q0);
+        const float4* st4 = reinterpret_cast<const float4*>(stile);
+        if (ok && a.out_dtype == 0) {
+            float4* gout = reinterpret_cast<float4*>(static_cast<float*>(a.out) + ((size_t)hq * S + q0) * kHeadDim);
+#pragma unroll 1
+            for (int c = tid; c < rows * 32; c += kConsumerThreads) gout[c] = st4[c ^ ((c >> 5) & 7)];
+        } else if (ok) {
+            // Output piece c (8 elements) = fp32 pieces 2p, 2p + 1 of its row.
+            uint4* gout = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + ((size_t)hq * S + q0) * kHeadDim);
+            const bool bf = a.out_dtype == 30;
+#pragma unroll 1
+            for (int c = tid; c < rows * 16; c += kConsumerThreads) {
+                const int row = c >> 4, p = c & 15;
+                const float4 x = st4[row * 32 + ((2 * p) ^ (row & 7))];
+                const float4 y = st4[row * 32 + ((2 * p + 1) ^ (row & 7))];
+                const uint4 w = bf ? make_uint4(bf16x2_rn(x.x, x.y), bf16x2_rn(x.z, x.w), bf16x2_rn(y.x, y.y),
+                                                bf16x2_rn(y.z, y.w))
+                                   : half8_rn(x, y);
+                gout[c] = w;
             }
         }
-        consumer_sync();
-        const int row_chunks = kHeadDim * es / 16;  // 16-byte pieces per row
-        const int rows = min(kBM, S - q0);
-        uint8_t* gout = static_cast<uint8_t*>(a.out) + ((size_t)hq * S + q0) * kHeadDim * es;
-        if (ok) {
-            for (int c = tid; c < rows * row_chunks; c += kConsumerThreads)
-                reinterpret_cast<uint4*>(gout)[c] = reinterpret_cast<const uint4*>(stile)[c];
-        }
     }
+    PROBE_EE(7);
     if (!ok) atomicOr(a.err, kErrTimeout);
     tc::fence_before_sync();
     __syncthreads();
