@@ -51,14 +51,18 @@ static_assert((9 + 4 * kStages) * 8 + 4 <= 256, "barriers and the TMEM slot fit 
 // (m, l) rows of the two softmax groups at the end: the last 4 KiB of the
 // last V stage.
 constexpr uint32_t kOffEx = kOffV + kStages * kTile - 4096;
-// Cluster merge: a sender's partials (O rows [128][128] fp32, then (m, l)
-// per row), one receive slot per other CTA of the cluster (up to 2) from
-// offset 0 of the leader; the output tile is staged after them.
+// Cluster reduce-scatter: a CTA's partials (O rows [128][128] fp32 at 0,
+// then (m, l, -, -) per row at kRecvO), one receive slot per other CTA of the
+// cluster (up to 2; each at most 64 rows of O then their (m, l, -, -)), and
+// the staged output rows (at most 128 x 512 bytes).
 constexpr uint32_t kRecvO = 128 * kHeadDim * 4;
-constexpr uint32_t kRecvSlot = kRecvO + 128 * 8;
-constexpr uint32_t kOffStage = (2 * kRecvSlot + 1023) / 1024 * 1024;
-static_assert(kOffStage + 128 * kHeadDim * 4 <= kOffEx, "staged output tile clear of the (m, l) exchange");
-static_assert(kRecvSlot % 16 == 0, "bulk copy size and slot offsets are multiples of 16 bytes");
+constexpr uint32_t kRowBytes = kHeadDim * 4 + 16;  // bytes received per row and sender
+constexpr uint32_t kRecvSlotO = 64 * kHeadDim * 4;
+constexpr uint32_t kRecvSlot = kRecvSlotO + 64 * 16;
+constexpr uint32_t kOffRecv = kRecvO + 128 * 16;
+constexpr uint32_t kOffStage = (kOffRecv + 2 * kRecvSlot + 1023) / 1024 * 1024;
+static_assert(kOffStage + 128 * kHeadDim * 4 <= kOffEx, "staged output rows clear of the (m, l) exchange");
+static_assert(kRecvSlot % 16 == 0 && kOffRecv % 16 == 0, "bulk copy addresses are multiples of 16 bytes");
 // TMEM columns: S/P of the two groups' tiles [0, 256) (buffer = tile & 1 =
 // group), O of group 0 [256, 384), O of group 1 [384, 512).
 constexpr uint32_t kTmemCols = 512;
@@ -595,65 +599,89 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
     m_run = Mg;
     l_run = (n_tiles > 0 ? l0 * f0 : 0.f) + (n_tiles > 1 ? l1 * f1 : 0.f);
-    float l_fin = l_run;
     PROBE_EE(5);
+    // Reduce-scatter over the cluster: CTA k finalises and stores query rows
+    // [k * 128 / n, (k + 1) * 128 / n). Each CTA writes the partials of the
+    // rows it does not own into its own (idle) shared memory and sends each
+    // other CTA that CTA's rows with bulk copies into its receive slot,
+    // completing on the receiver's bar_recv. Per-thread st.shared::cluster
+    // stores of the same bytes ran at ~10 B/clk; a leader receiving every
+    // row took 1.7 us for the copy alone.
+    const int row_lo = rank * kBM / n_split, row_hi = (rank + 1) * kBM / n_split;
+    const bool own = r >= row_lo && r < row_hi;
+    float l_fin = l_run;
     if (n_split > 1) {
-        // Merge through distributed shared memory. Each other CTA of the
-        // cluster writes its (O row, m, l) partials into its own (now idle)
-        // shared memory and sends them with ONE bulk copy into the leader's
-        // receive slot, completing on the leader's bar_recv: per-thread
-        // st.shared::cluster stores of the same 64 KiB ran at ~10 B/clk
-        // (~3 us), the bulk copy at the DSMEM link rate. Rows are 512 bytes
-        // apart, so the 16-byte pieces of a row are XOR-permuted by the
-        // row's low 3 bits: the 8 threads of one shared-memory phase
-        // (consecutive rows) then hit distinct banks.
-        const uint32_t row_off = r * kHeadDim * 4 + hc * 64 * 4;
-        if (rank == 0 && tid == 0) mbar_arrive_expect_tx(bar_recv, (n_split - 1) * kRecvSlot);
-        if (rank > 0) {
-            float4* mine = reinterpret_cast<float4*>(smem + row_off);
+        // Partials: O rows [128][128] fp32 at offset 0, 16-byte pieces
+        // XOR-permuted by the row's low 3 bits (rows are 512 bytes apart; the
+        // 8 threads of a shared-memory phase then hit distinct banks), and
+        // (m, l, -, -) per row at kRecvO.
+        if (!own) {
+            float4* mine = reinterpret_cast<float4*>(smem + r * kHeadDim * 4 + hc * 64 * 4);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                mine[i ^ (r & 7)] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-            if (hc == 0) reinterpret_cast<float2*>(smem + kRecvO)[r] = make_float2(m_run, l_run);
+            for (int i = 0; i < 16; ++i) mine[i ^ (r & 7)] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            if (hc == 0) reinterpret_cast<float4*>(smem + kRecvO)[r] = make_float4(m_run, l_run, 0.f, 0.f);
             fence_proxy_async_smem();
         }
+        if (tid == 0) mbar_arrive_expect_tx(bar_recv, (uint32_t)((n_split - 1) * (row_hi - row_lo)) * kRowBytes);
         // Every CTA's MMAs are done (its shared memory may be overwritten) and
-        // the senders' partials are written.
+        // its partials are written.
         tc::fence_before_sync();
         asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
         PROBE_EE(8);
-        if (rank > 0 && tid == 0) {
-            uint32_t dst, bar;
-            const uint32_t ldst = smem_addr(smem + (rank - 1) * kRecvSlot);
-            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(dst) : "r"(ldst));
-            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(bar) : "r"(smem_addr(bar_recv)));
-            asm volatile(
-                "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n\t"
-                "cp.async.bulk.commit_group;" ::"r"(dst),
-                "r"(smem_addr(smem)), "r"(kRecvSlot), "r"(bar)
-                : "memory");
+        if (tid == 0) {
+            for (int d = 0; d < n_split; ++d) {
+                if (d == rank) continue;
+                const int lo = d * kBM / n_split, n = (d + 1) * kBM / n_split - lo;
+                const uint32_t slot = kOffRecv + (uint32_t)(rank < d ? rank : rank - 1) * kRecvSlot;
+                uint32_t dst_o, dst_ml, bar;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst_o) : "r"(smem_addr(smem + slot)), "r"(d));
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                             : "=r"(dst_ml)
+                             : "r"(smem_addr(smem + slot + kRecvSlotO)), "r"(d));
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_addr(bar_recv)), "r"(d));
+                // The O rows in 4 pieces (several copies in flight), then (m, l).
+                const uint32_t ob = (uint32_t)n * kHeadDim * 4, piece = (ob / 4 + 15) / 16 * 16;
+                for (uint32_t off = 0; off < ob; off += piece) {
+                    const uint32_t bytes = ob - off < piece ? ob - off : piece;
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                            dst_o + off),
+                        "r"(smem_addr(smem + (uint32_t)lo * kHeadDim * 4 + off)), "r"(bytes), "r"(bar)
+                        : "memory");
+                }
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        dst_ml),
+                    "r"(smem_addr(smem + kRecvO + (uint32_t)lo * 16)), "r"((uint32_t)n * 16), "r"(bar)
+                    : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             PROBE_EE(9);
-            // The source must stay valid until the copy has read it.
+            // The sources must stay valid until the copies have read them.
             asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         }
-        // Waited for even after an earlier timeout: the leader must not exit
+        // Waited for even after an earlier timeout: the CTA must not exit
         // while copies into its shared memory are in flight.
-        if (rank == 0 && !mbar_wait_bounded(bar_recv, 0)) ok = false;
+        if (!mbar_wait_bounded(bar_recv, 0)) ok = false;
         PROBE_EE(10);
-        if (rank == 0) {
+        if (own) {
+            const int lr = r - row_lo;  // row within the received slots
             float M = m_run;
-            for (int k = 1; k < n_split; ++k)
-                M = fmaxf(M, reinterpret_cast<const float2*>(smem + (k - 1) * kRecvSlot + kRecvO)[r].x);
+            for (int k = 0; k < n_split - 1; ++k)
+                M = fmaxf(M, reinterpret_cast<const float4*>(smem + kOffRecv + k * kRecvSlot + kRecvSlotO)[lr].x);
             const float Ms = M == -INFINITY ? 0.f : M;
             const float f0 = exp2_approx(m_run - Ms);
             l_fin = l_run * f0;
 #pragma unroll
             for (int i = 0; i < 64; ++i) o[i] *= f0;
-            for (int k = 1; k < n_split; ++k) {
-                const float2 ml = reinterpret_cast<const float2*>(smem + (k - 1) * kRecvSlot + kRecvO)[r];
+            for (int k = 0; k < n_split - 1; ++k) {
+                const float4 ml = reinterpret_cast<const float4*>(smem + kOffRecv + k * kRecvSlot + kRecvSlotO)[lr];
                 const float f = exp2_approx(ml.x - Ms);
                 l_fin = fmaf(ml.y, f, l_fin);
-                const float4* src = reinterpret_cast<const float4*>(smem + (k - 1) * kRecvSlot + row_off);
+                // The sender's layout: row lo + lr of its buffer, pieces
+                // permuted by that row's (= r's) low 3 bits.
+                const float4* src =
+                    reinterpret_cast<const float4*>(smem + kOffRecv + k * kRecvSlot + lr * kHeadDim * 4 + hc * 64 * 4);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const float4 v = src[i ^ (r & 7)];
@@ -671,49 +699,48 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 #endif
     PROBE_EE(6);
     const float inv = 1.f / l_fin;
-#ifdef GKV_PROBE_TIMELINE
-    asm volatile("" ::"f"(inv));
-    PROBE_EE(13);
-#endif
-    // Output tile [128 queries][128 dims] through shared memory (idle stage
-    // buffers clear of the merge's receive slots): each thread alone holds
-    // 64 elements of one row, and rows are 256 or 512 bytes apart, so direct
-    // stores would touch a new line per lane. The normalised fp32 rows are
-    // staged first (16-byte pieces XOR-permuted by the row's low 3 bits:
-    // bank-conflict free on both sides, as in the merge); then a compact loop
-    // converts to the output dtype with consecutive threads on consecutive
-    // 16-byte pieces of the output. This code runs once per CTA from a cold
-    // instruction cache, so it is kept short: a fully unrolled conversion of
-    // the 64 register values cost ~2 us per CTA, and time grew with the code
-    // size of the conversion rather than with its instruction count.
-    if (rank == 0) {
-        uint8_t* stile = smem + kOffStage;
-        float4* mine = reinterpret_cast<float4*>(stile + r * kHeadDim * 4 + hc * 64 * 4);
+    // This CTA's output rows through shared memory (clear of the partials
+    // and the receive slots): each thread alone holds 64 elements of one row,
+    // and rows are 256 or 512 bytes apart, so direct stores would touch a
+    // new line per lane. The normalised fp32 rows are staged first (pieces
+    // permuted as above); then a compact loop converts to the output dtype
+    // with consecutive threads on consecutive 16-byte pieces of the output.
+    // This code runs once per CTA from a cold instruction cache, so it is
+    // kept short: a fully unrolled conversion of the 64 register values cost
+    // ~2 us per CTA, and time grew with the code size of the conversion
+    // rather than with its instruction count.
+    uint8_t* stile = smem + kOffStage;
+    if (own) {
+        float4* mine = reinterpret_cast<float4*>(stile + (r - row_lo) * kHeadDim * 4 + hc * 64 * 4);
 #pragma unroll
         for (int i = 0; i < 16; ++i)
             mine[i ^ (r & 7)] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-        PROBE_EE(11);
-        consumer_sync();
-        PROBE_EE(12);
-        const int rows = min(kBM, S - q0);
+    }
+    PROBE_EE(11);
+    consumer_sync();
+    PROBE_EE(12);
+    {
+        const int rows = min(row_hi, S - q0) - row_lo;  // this CTA's rows inside the chunk
         const float4* st4 = reinterpret_cast<const float4*>(stile);
-        if (ok && a.out_dtype == 0) {
-            float4* gout = reinterpret_cast<float4*>(static_cast<float*>(a.out) + ((size_t)hq * S + q0) * kHeadDim);
+        const size_t row0 = (size_t)hq * S + q0 + row_lo;
+        if (ok && rows > 0 && a.out_dtype == 0) {
+            float4* gout = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row0 * kHeadDim);
 #pragma unroll 1
-            for (int c = tid; c < rows * 32; c += kConsumerThreads) gout[c] = st4[c ^ ((c >> 5) & 7)];
-        } else if (ok) {
+            for (int c = tid; c < rows * 32; c += kConsumerThreads) {
+                const int lr = c >> 5;
+                gout[c] = st4[lr * 32 + ((c & 31) ^ ((lr + row_lo) & 7))];
+            }
+        } else if (ok && rows > 0) {
             // Output piece c (8 elements) = fp32 pieces 2p, 2p + 1 of its row.
-            uint4* gout = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + ((size_t)hq * S + q0) * kHeadDim);
+            uint4* gout = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + row0 * kHeadDim);
             const bool bf = a.out_dtype == 30;
 #pragma unroll 1
             for (int c = tid; c < rows * 16; c += kConsumerThreads) {
-                const int row = c >> 4, p = c & 15;
-                const float4 x = st4[row * 32 + ((2 * p) ^ (row & 7))];
-                const float4 y = st4[row * 32 + ((2 * p + 1) ^ (row & 7))];
-                const uint4 w = bf ? make_uint4(bf16x2_rn(x.x, x.y), bf16x2_rn(x.z, x.w), bf16x2_rn(y.x, y.y),
-                                                bf16x2_rn(y.z, y.w))
-                                   : half8_rn(x, y);
-                gout[c] = w;
+                const int lr = c >> 4, p = c & 15, sw = (lr + row_lo) & 7;
+                const float4 x = st4[lr * 32 + ((2 * p) ^ sw)];
+                const float4 y = st4[lr * 32 + ((2 * p + 1) ^ sw)];
+                gout[c] = bf ? make_uint4(bf16x2_rn(x.x, x.y), bf16x2_rn(x.z, x.w), bf16x2_rn(y.x, y.y), bf16x2_rn(y.z, y.w))
+                             : half8_rn(x, y);
             }
         }
     }
