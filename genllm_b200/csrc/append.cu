@@ -27,6 +27,7 @@ struct AppendParams {
     int32_t pool_pages;
     int32_t new_first;
     int32_t new_n;
+    int32_t pdl;  // kAppendDependent | kAppendTrigger
     int2 new_ids[kMaxNewPagesPerLaunch];
 };
 
@@ -38,6 +39,10 @@ constexpr int kAppendWarps = 4;
 // (the source does not depend on it), so the two latencies overlap; then it
 // stores them in slot order (consecutive lanes, consecutive bytes).
 __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const AppendParams a) {
+    // As a programmatic dependent: nothing of the previous kernel's output
+    // (pages, table, the K/V source) is touched before it has completed.
+    if (a.pdl & kAppendDependent) asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (a.pdl & kAppendTrigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (blockIdx.x == 0 && (int)threadIdx.x < a.new_n)
         a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
 
@@ -91,7 +96,7 @@ __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const Appe
 cudaError_t launch_append(const PoolView& pool, int2* table, const NewPages& np,
                           const uint16_t* k, const uint16_t* v, int32_t n_prior,
                           int32_t src_len, int32_t p_begin, int32_t p_end, uint32_t* err,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, int pdl) {
     AppendParams a;
     a.k = reinterpret_cast<const uint4*>(k);
     a.v = reinterpret_cast<const uint4*>(v);
@@ -107,12 +112,25 @@ cudaError_t launch_append(const PoolView& pool, int2* table, const NewPages& np,
     a.pool_pages = pool.pool_pages;
     a.new_first = np.first;
     a.new_n = np.n;
+    a.pdl = pdl;
     for (int i = 0; i < np.n; ++i) a.new_ids[i] = np.ids[i];
     long long blocks = (2ll * a.count + kAppendWarps - 1) / kAppendWarps;
     if (blocks < 1) blocks = 1;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    kv_append_kernel<<<(unsigned)blocks, kAppendWarps * 32, 0, stream>>>(a);
-    return cudaGetLastError();
+    if (!(pdl & kAppendDependent)) {
+        kv_append_kernel<<<(unsigned)blocks, kAppendWarps * 32, 0, stream>>>(a);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(kAppendWarps * 32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kv_append_kernel, a);
 }
 
 }  // namespace gkv

@@ -315,8 +315,11 @@ int publish(const gkv_pool_desc* pool, gkv_table* t, const gkv_new_pages* np, in
     return GKV_OK;
 }
 
+// for_prefill: the chunked-prefill kernel follows (it waits for the
+// appends): the appends are launched as programmatic dependents and the last
+// one lets the prefill start its launch and setup early.
 int append_chunks(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, const gkv_new_pages* np,
-                  const void* K, const void* V, int32_t seq_len, cudaStream_t s) {
+                  const void* K, const void* V, int32_t seq_len, cudaStream_t s, bool for_prefill = false) {
     gkv::PoolView pv{static_cast<uint16_t*>(pool->k_base), static_cast<uint16_t*>(pool->v_base),
                      pool->pool_pages, pool->n_kv_heads};
     // Launch in chunks of at most 64 pages (1024 tokens) so that each launch's
@@ -339,9 +342,11 @@ int append_chunks(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
             published = to;
         }
         gkv::NewPages p = pack(np, published, upto - published);
+        const bool last = c1 >= seq_len && upto >= n_new;
+        const int pdl = for_prefill ? gkv::kAppendDependent | (last ? gkv::kAppendTrigger : 0) : 0;
         cudaError_t e = gkv::launch_append(pv, t->d_table, p, static_cast<const uint16_t*>(K),
                                            static_cast<const uint16_t*>(V), n_prior, seq_len, c0, c1,
-                                           t->scratch.err, s);
+                                           t->scratch.err, s, pdl);
         if (e != cudaSuccess) return cuda_fail(e, "append launch");
         published = upto;
     }
@@ -597,7 +602,7 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
 
     {
         NvtxRange nvtx_range("gkv chunk append");
-        if ((st = append_chunks(pool, t, n_prior, np, K, V, seq_len, s))) return st;
+        if ((st = append_chunks(pool, t, n_prior, np, K, V, seq_len, s, !prefill_on_cuda_cores()))) return st;
     }
     NvtxRange nvtx_range("gkv chunk attention");
     gkv::PrefillLaunch pl{};

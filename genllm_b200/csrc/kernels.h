@@ -155,11 +155,16 @@ cudaError_t launch_import_fp8(const PoolView& pool, const int2* table, int32_t n
 
 // Scatter tokens [p_begin, p_end) of K/V ([Hkv][src_len][128]) to positions
 // n_prior + p, and publish np's entries to the table. With p_begin == p_end
-// only the table entries are written.
+// only the table entries are written. pdl: kAppendDependent launches it as a
+// programmatic dependent of the previous kernel (it waits for that kernel
+// before touching memory); kAppendTrigger lets the next kernel, which must be
+// one that waits for it likewise (the chunked-prefill kernel), start its
+// launch and setup while this one runs.
+constexpr int kAppendDependent = 1, kAppendTrigger = 2;
 cudaError_t launch_append(const PoolView& pool, int2* table, const NewPages& np,
                           const uint16_t* k, const uint16_t* v, int32_t n_prior,
                           int32_t src_len, int32_t p_begin, int32_t p_end, uint32_t* err,
-                          cudaStream_t stream);
+                          cudaStream_t stream, int pdl = 0);
 
 struct PrefillLaunch {
     const uint16_t* q;  // [Hq][S][128]

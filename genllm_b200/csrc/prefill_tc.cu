@@ -7,24 +7,27 @@
 // (src/backend/cpu/attention.cpp:156-215). Here a chunk of S queries of one
 // query head attends causally over every cached page:
 //
-//   * CTA = 128 queries x 1 query head (grid ceil(S/128) x Hq), 8 warps; warp
-//     w owns TMEM lanes [32(w%4), +32): two threads per query row, each with
-//     64 of the 128 key columns of a tile (they exchange their partial max /
-//     sum through spare TMEM columns);
+//   * CTA = 128 queries x 1 query head (grid ceil(S/128) x Hq [x KV split]),
+//     11 warps: two softmax groups of 4 warps, a K-load warp, a V-load warp
+//     and an MMA warp;
 //   * Q tile [128 x 128] and each KV tile (128 keys = 8 pages of 16 slots)
-//     arrive by TMA in the 128-byte-swizzled K-major layout: per page and
-//     per 64-dim half one box {64 dims, 1 head, 16 slots} of the pool's 3-D
-//     map; K and V tiles are double-buffered;
-//   * S = Q K^T: 8 tcgen05.mma (M128 N128 K16, bf16 -> fp32) into TMEM
-//     columns [0, 128), issued by one thread, completion by tcgen05.commit;
-//   * each thread loads its S row from TMEM, applies the causal / length
-//     mask, and updates an fp32 online softmax (log2 domain); the
-//     probabilities go to shared memory as bf16 in the swizzled K-major
-//     layout; O in TMEM columns [128, 256) is rescaled in place when the
-//     running max moves;
-//   * O += P V: 16 tcgen05.mma with V as an MN-major operand — P enters as
-//     bf16 hi + lo terms so that the products keep fp32-level accuracy;
-//   * the epilogue divides by the row sum and stores fp32/bf16/fp16 rows.
+//     arrive by TMA in the 128-byte-swizzled K-major layout (one box per
+//     page and 64-dim half, or one box per 8-page run of consecutive ids);
+//     K and V tiles sit in 3-stage rings;
+//   * the KV tiles alternate between the two softmax groups; group g owns
+//     S/P buffer g (TMEM columns [128 g, +128)) and O accumulator g
+//     ([256 + 128 g, +128)), one thread per query row;
+//   * S = Q K^T: 8 tcgen05.mma (M128 N128 K16, bf16 -> fp32), both operands
+//     in shared memory, issued by one thread, completion by tcgen05.commit;
+//   * each group thread loads its S row from TMEM, applies the causal /
+//     length mask, updates an fp32 online softmax (log2 domain, lazy
+//     rescaling) and stores P over S in TMEM as bf16 hi + lo terms, so that
+//     O_g += P V (16 tcgen05.mma, V an MN-major operand) keeps fp32-level
+//     accuracy; while one group computes, the tensor cores run the other's
+//     MMAs;
+//   * the groups' (m, l, O) are merged, then the CTAs of a KV-split cluster
+//     reduce-scatter their partials through distributed shared memory, and
+//     each stores its share of the rows (fp32/bf16/fp16).
 //
 // Keys past the cached length in the last tile are masked in S, and their V
 // rows are zeroed in shared memory (0 x NaN from stale slots would poison
@@ -230,6 +233,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // Launched as a programmatic dependent: the setup above overlapped the
+    // previous kernel (the chunk's append); nothing it writes (pages, table)
+    // or that came before it (Q) is read until it has completed.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     PROBE_EE(1);
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
@@ -397,6 +404,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         if (n_split > 1)  // the consumers' cluster barrier (every CTA's MMAs done)
             asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
         tc::fence_before_sync();
@@ -430,6 +438,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         if (n_split > 1)  // the consumers' cluster barrier (every CTA's MMAs done)
             asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
         tc::fence_before_sync();
@@ -600,6 +609,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     m_run = Mg;
     l_run = (n_tiles > 0 ? l0 * f0 : 0.f) + (n_tiles > 1 ? l1 * f1 : 0.f);
     PROBE_EE(5);
+    // The next kernel may start launching (a kernel that does not wait for
+    // this one is never launched as its programmatic dependent).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Reduce-scatter over the cluster: CTA k finalises and stores query rows
     // [k * 128 / n, (k + 1) * 128 / n). Each CTA writes the partials of the
     // rows it does not own into its own (idle) shared memory and sends each
@@ -781,13 +793,15 @@ cudaError_t launch_tc(const CUtensorMap& q_map, const PoolMaps& maps, const TcPa
     cfg.blockDim = dim3(kThreadsTc);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = n_split;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, maps.k, maps.v, maps.k_run, maps.v_run, a);
 }
 }  // namespace
