@@ -327,7 +327,7 @@ def measure_config1(args):
 def measure_config4(args):
     """Config 4 (chunked prefill on the tensor cores) for the bench line:
     causal-exact TFLOP/s over an 8192-token prompt in 512-token chunks."""
-    return prefill_numbers(argparse.Namespace(steps=3, warmup=2))
+    return prefill_numbers(argparse.Namespace(steps=20, warmup=3))
 
 
 # --------------------------------------------------------------------------
