@@ -201,8 +201,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
-    const int q0 = blockIdx.x * kBM;
-    const int hq = blockIdx.y;
+    // Longest work first: CTAs start in the order of their linear index (x
+    // fastest), which is mapped to (query tile, head) with the heads
+    // innermost and the query tiles descending, so that under a causal mask
+    // the CTAs with the most KV tiles start first and the last wave holds
+    // the shortest ones.
+    const int lin = blockIdx.y * gridDim.x + blockIdx.x;
+    const int hq = lin % gridDim.y;
+    const int q0 = (gridDim.x - 1 - lin / gridDim.y) * kBM;
     const int G = a.n_q_heads / a.n_kv_heads;
     // Paged: blockIdx.y is the query head. Contiguous (non-paged attention
     // over B sequences): blockIdx.y = b * Hq + head, and the K/V rows of
