@@ -65,12 +65,17 @@ class HeadGather:
         self.handle = g
         raw = torch.as_tensor(_CudaArray(out.value, (n_layers * n_q_heads * head_dim * self.esize // 2,), "<i2"),
                               device=f"cuda:{device}")
-        # This rank's gathered outputs; valid until close().
+        # This rank's gathered outputs (memory valid until close()). full[l]
+        # holds layer l's latest step only until layer l's next gather call on
+        # any rank: a peer's next call stores over it as soon as that peer
+        # gets there, so read it (stream-ordered) before this rank's next call
+        # for the same layer (gkv_paged_attention_gather in genllm_kv.h).
         self.full = raw.view(dtype).view(n_layers, n_q_heads, head_dim)
         dist.barrier(group=group)
 
     def decode(self, manager, layer_id: int, Q, K, V, scale: float, stream=None) -> torch.Tensor:
-        """Decode step of this rank's heads; returns the full [Hq, D] output of the layer."""
+        """Decode step of this rank's heads; returns the full [Hq, D] output of the layer (a view that
+        the layer's next call on any rank overwrites)."""
         hq_local = Q.shape[1]
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         code = {torch.bfloat16: _lib.GKV_BF16, torch.float16: _lib.GKV_F16, torch.float32: _lib.GKV_F32}[self.dtype]
