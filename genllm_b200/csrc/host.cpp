@@ -219,6 +219,16 @@ struct gkv_table {
     };
     QMap qmaps[16];
     int qmap_next = 0;
+    // The same for the chunk's K/V inputs (the prefill reads the chunk's own
+    // tiles from them), keyed by (K, V, heads, rows).
+    struct KvMap {
+        const void* k = nullptr;
+        const void* v = nullptr;
+        int32_t heads = 0, rows = 0;
+        CUtensorMap maps[2];
+    };
+    KvMap kvmaps[16];
+    int kvmap_next = 0;
 };
 
 namespace {
@@ -633,6 +643,27 @@ int attention_raw(const gkv_pool_desc* pool, gkv_table* t, int32_t n_prior, cons
             e.rows = seq_len;
             q_map = &e.map;
         }
+        // The chunk's K/V inputs as tensor maps (16-byte aligned inputs only).
+        const CUtensorMap* kv_new = nullptr;
+        if ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) % 16 == 0) {
+            for (const auto& e : t->kvmaps)
+                if (e.k == K && e.v == V && e.heads == pool->n_kv_heads && e.rows == seq_len) kv_new = e.maps;
+            if (!kv_new) {
+                auto& e = t->kvmaps[t->kvmap_next];
+                t->kvmap_next = (t->kvmap_next + 1) % 16;
+                const char* why = nullptr;
+                e.k = e.v = nullptr;
+                if (gkv::encode_contig_kv_maps_sw128(static_cast<const uint16_t*>(K), static_cast<const uint16_t*>(V),
+                                                     seq_len, pool->n_kv_heads, &e.maps[0], &e.maps[1], &why)) {
+                    e.k = K;
+                    e.v = V;
+                    e.heads = pool->n_kv_heads;
+                    e.rows = seq_len;
+                    kv_new = e.maps;
+                }
+            }
+        }
+        pl.kv_new = kv_new;
         const gkv::PoolMaps maps{t->k_map_sw, t->v_map_sw, t->runs ? t->k_map_run : t->k_map_sw,
                                  t->runs ? t->v_map_run : t->v_map_sw, t->runs};
         e = gkv::launch_prefill_tc(pv, *q_map, maps, t->d_table, pl, t->scratch.err, t->num_sms, s);

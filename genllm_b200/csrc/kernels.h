@@ -176,6 +176,12 @@ struct PrefillLaunch {
     int32_t n_pages;
     float scale;
     int32_t causal;
+    // Tensor-core prefill only: tensor maps {K, V} over the chunk's inputs
+    // ([Hkv][S][128], box {64, 128, 1}). When given and the chunk starts on a
+    // 128-token tile boundary, the chunk's own KV tiles are read from them
+    // rather than from the pages, and the launch waits for the preceding
+    // append only before it completes, so the two run side by side.
+    const CUtensorMap* kv_new = nullptr;
 };
 
 // Per-head QK-norm + RoPE of Q and K and the head-major permute of Q, K and

@@ -32,6 +32,8 @@
 // Keys past the cached length in the last tile are masked in S, and their V
 // rows are zeroed in shared memory (0 x NaN from stale slots would poison
 // the MMA). Every mbarrier wait is bounded (kErrTimeout).
+#include <climits>
+
 #include "device.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -85,6 +87,15 @@ struct TcParams {
     int32_t causal;
     int32_t runs;    // k_run / v_run maps usable
     int32_t contig;  // 1: K/V are contiguous [B*Hkv][S][128] (k_run / v_run map them), no table
+    // KV tiles with index >= new_tile0 hold only this chunk's tokens and are
+    // copied from the chunk's K/V inputs ([Hkv][S][128], k_new / v_new) at
+    // row (tile - new_tile0) * 128 instead of from the pages (INT_MAX: none).
+    int32_t new_tile0;
+    // 1: every input this launch reads was complete before the previous
+    // kernel (the chunk's append) started, so the launch does not wait for
+    // it before reading, only before it completes (the next chunk reads the
+    // pages that append writes).
+    int32_t wait_at_end;
     float qscale;    // softmax scale * log2(e)
 };
 
@@ -183,7 +194,8 @@ __device__ __noinline__ uint4 half8_rn(float4 x, float4 y) {
 __global__ void __launch_bounds__(kThreadsTc, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                       const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap k_run,
-                      const __grid_constant__ CUtensorMap v_run, const TcParams a) {
+                      const __grid_constant__ CUtensorMap v_run, const __grid_constant__ CUtensorMap k_new,
+                      const __grid_constant__ CUtensorMap v_new, const TcParams a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -240,9 +252,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     __syncthreads();
     tc::fence_after_sync();
     // Launched as a programmatic dependent: the setup above overlapped the
-    // previous kernel (the chunk's append); nothing it writes (pages, table)
-    // or that came before it (Q) is read until it has completed.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // previous kernel (the chunk's append). Unless the launch takes the
+    // chunk's own tiles from its inputs (wait_at_end), nothing that kernel
+    // writes (pages, table) or that came before it (Q) is read until it has
+    // completed.
+    if (!a.wait_at_end) asm volatile("griddepcontrol.wait;" ::: "memory");
     PROBE_EE(1);
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
@@ -263,7 +277,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         for (int i = 0; i < kPagesPerTile; ++i) {
             int lp = (j0 + j) * kPagesPerTile + i;
             if (lp >= a.n_pages) lp = a.n_pages - 1;  // beyond the cache: rows are masked / zeroed
-            e[i] = a.table[lp];
+            // The chunk's own tiles come from its inputs; their entries may
+            // still be in the append's hands.
+            e[i] = j0 + j >= a.new_tile0 ? make_int2(0, 0) : a.table[lp];
         }
     };
     // Stage tile j's K (which = 0) or V (which = 1) into stage j % kStages.
@@ -281,6 +297,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             for (int hf = 0; hf < 2; ++hf)
                 tma_load_3d(smem + (which ? kOffV : kOffK) + st * kTile + hf * kHalf, which ? &v_run : &k_run, bar,
                             hf * 64, (j0 + j) * kBN, h, pol_kv);
+            return;
+        }
+        if (j0 + j >= a.new_tile0) {  // the chunk's own keys, from its inputs (past S: zero-filled)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+                tma_load_3d(smem + (which ? kOffV : kOffK) + st * kTile + hf * kHalf, which ? &v_new : &k_new, bar,
+                            hf * 64, (j0 + j - a.new_tile0) * kBN, h, pol_kv);
             return;
         }
         const int mode = tile_mode_regs(ids, a.pool_pages, a.runs);
@@ -461,7 +484,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     // next tile (fetched a tile ahead) to derive its copy mode.
     const int lane = tid & 31;
     auto entry = [&](int j) {
-        if (a.contig) return make_int2(-1, -1);  // no table: every tile is in key order (mode 0)
+        // No table (contiguous K/V, or the chunk's own tiles from its
+        // inputs): the tile is in key order (mode 0).
+        if (a.contig || j0 + j >= a.new_tile0) return make_int2(-1, -1);
         int lp = (j0 + j) * kPagesPerTile + (lane & (kPagesPerTile - 1));
         if (lp >= a.n_pages) lp = a.n_pages - 1;
         return a.table[lp];
@@ -764,6 +789,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
     PROBE_EE(7);
     if (!ok) atomicOr(a.err, kErrTimeout);
+    // The grid completes only after the previous kernel has (whatever reads
+    // this launch's output, or the pages that kernel wrote, waits for this
+    // one).
+    if (a.wait_at_end && tid == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
     tc::fence_before_sync();
     __syncthreads();
     PROBE_EE(3);
@@ -779,8 +808,8 @@ namespace {
 // Launch prefill_tc_kernel over `rows` query rows of `heads` (query heads, or
 // sequences x query heads), splitting the KV range over a cluster of up to 3
 // CTAs while the query tiles alone would leave SMs idle.
-cudaError_t launch_tc(const CUtensorMap& q_map, const PoolMaps& maps, const TcParams& a, int rows, int heads,
-                      int num_sms, cudaStream_t stream) {
+cudaError_t launch_tc(const CUtensorMap& q_map, const PoolMaps& maps, const CUtensorMap* new_maps, const TcParams& a,
+                      int rows, int heads, int num_sms, cudaStream_t stream) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -808,7 +837,8 @@ cudaError_t launch_tc(const CUtensorMap& q_map, const PoolMaps& maps, const TcPa
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, maps.k, maps.v, maps.k_run, maps.v_run, a);
+    return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q_map, maps.k, maps.v, maps.k_run, maps.v_run,
+                              new_maps ? new_maps[0] : maps.k, new_maps ? new_maps[1] : maps.v, a);
 }
 }  // namespace
 
@@ -829,8 +859,14 @@ cudaError_t launch_prefill_tc(const PoolView& pool, const CUtensorMap& q_map, co
     a.causal = p.causal;
     a.runs = maps.runs ? 1 : 0;
     a.contig = 0;
+    // The chunk's own tiles from its inputs: only when the chunk starts on a
+    // tile boundary (every tile is then all old or all new keys).
+    const int32_t n_prior = p.total - p.seq_len;
+    const bool from_inputs = p.kv_new != nullptr && n_prior % kBN == 0;
+    a.new_tile0 = from_inputs ? n_prior / kBN : INT_MAX;
+    a.wait_at_end = from_inputs ? 1 : 0;
     a.qscale = p.scale * 1.4426950408889634f;
-    return launch_tc(q_map, maps, a, p.seq_len, p.n_q_heads, num_sms, stream);
+    return launch_tc(q_map, maps, from_inputs ? p.kv_new : nullptr, a, p.seq_len, p.n_q_heads, num_sms, stream);
 }
 
 cudaError_t launch_flash_tc(const CUtensorMap& q_map, const CUtensorMap& k_map, const CUtensorMap& v_map,
@@ -849,9 +885,11 @@ cudaError_t launch_flash_tc(const CUtensorMap& q_map, const CUtensorMap& k_map, 
     a.causal = f.causal;
     a.runs = 0;
     a.contig = 1;
+    a.new_tile0 = INT_MAX;
+    a.wait_at_end = 0;
     a.qscale = f.scale * 1.4426950408889634f;
     const PoolMaps maps{k_map, v_map, k_map, v_map, false};
-    return launch_tc(q_map, maps, a, f.seq_len, f.batch * f.n_q_heads, num_sms, stream);
+    return launch_tc(q_map, maps, nullptr, a, f.seq_len, f.batch * f.n_q_heads, num_sms, stream);
 }
 
 }  // namespace gkv
