@@ -74,8 +74,12 @@ def test_poisoned_unused_slots():
 
 
 @pytest.mark.parametrize("n_prior,n_new,causal", [(0, 1, True), (5, 40, True), (16, 16, True), (100, 77, False),
-                                                  (3, 600, True)])
+                                                  (3, 600, True), (128, 200, True), (256, 77, False),
+                                                  (640, 129, True)])
 def test_chunk_paths(n_prior, n_new, causal):
+    """Chunks that start on a 128-token tile boundary read their own KV tiles
+    from the chunk's inputs (the append runs beside the attention); the
+    others read every tile from the pages."""
     case = fragmented_case(300 + n_new, 16, 8, 128, n_prior, (n_prior + n_new) // 16 + 4, n_new=n_new)
     check_case(case, causal)
 
@@ -90,9 +94,12 @@ def test_chunk_group_sizes(g, hkv, causal):
     check_case(case, causal)
 
 
-def test_long_chunk_over_1024_tokens():
-    """Chunks longer than one append launch carries (64 pages) are split."""
-    case = fragmented_case(77, 4, 2, 128, 40, 200, n_new=1500)
+@pytest.mark.parametrize("n_prior", [40, 128])
+def test_long_chunk_over_1024_tokens(n_prior):
+    """Chunks longer than one append launch carries (64 pages) are split
+    (from a tile boundary: several appends, the last one beside the
+    attention)."""
+    case = fragmented_case(77, 4, 2, 128, n_prior, 200, n_new=1500)
     check_case(case, True)
 
 
