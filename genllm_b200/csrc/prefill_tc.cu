@@ -238,6 +238,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int n_tiles = (rank + 1) * n_tiles_all / n_split - j0;
 
     PROBE_EE(0);
+    // The load warps fetch the first tile's page ids before the setup below
+    // when nothing the previous kernel writes is read (wait_at_end): the
+    // table load's latency then overlaps TMEM allocation and barrier setup.
+    int2 ids_pre[kPagesPerTile];
+    const bool pre = (warp == kLoadWarp || warp == kLoadWarp + 1) && (tid & 31) == 0 && n_tiles > 0 && !a.contig &&
+                     a.wait_at_end;
+    if (pre) {
+#pragma unroll
+        for (int i = 0; i < kPagesPerTile; ++i) {
+            int lp = j0 * kPagesPerTile + i;
+            if (lp >= a.n_pages) lp = a.n_pages - 1;
+            ids_pre[i] = j0 >= a.new_tile0 ? make_int2(0, 0) : a.table[lp];
+        }
+    }
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
@@ -451,7 +465,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
             uint64_t* freed = which ? bar_vfree : bar_kfree;
             int2 ids[kPagesPerTile], nxt[kPagesPerTile];
-            if (n_tiles > 0 && !a.contig) load_ids(0, ids);
+            if (pre) {
+#pragma unroll
+                for (int i = 0; i < kPagesPerTile; ++i) ids[i] = ids_pre[i];
+            } else if (n_tiles > 0 && !a.contig) {
+                load_ids(0, ids);
+            }
             for (int j = 0; j < n_tiles && ok; ++j) {
                 if (j + 1 < n_tiles && !a.contig) load_ids(j + 1, nxt);
                 if (which == 0) { PROBE_LD(0); }
