@@ -39,10 +39,13 @@ constexpr int kAppendWarps = 4;
 // (the source does not depend on it), so the two latencies overlap; then it
 // stores them in slot order (consecutive lanes, consecutive bytes).
 __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const AppendParams a) {
+    // The chunked-prefill kernel that follows may start at once: it waits for
+    // this kernel before it reads anything this kernel writes (or, reading
+    // the chunk's own tiles from the inputs, before its output stores).
+    if (a.pdl & kAppendTrigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // As a programmatic dependent: nothing of the previous kernel's output
     // (pages, table, the K/V source) is touched before it has completed.
     if (a.pdl & kAppendDependent) asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (a.pdl & kAppendTrigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (blockIdx.x == 0 && (int)threadIdx.x < a.new_n)
         a.table[a.new_first + threadIdx.x] = a.new_ids[threadIdx.x];
 
@@ -117,6 +120,10 @@ cudaError_t launch_append(const PoolView& pool, int2* table, const NewPages& np,
     long long blocks = (2ll * a.count + kAppendWarps - 1) / kAppendWarps;
     if (blocks < 1) blocks = 1;
     if (blocks > 148 * 16) blocks = 148 * 16;
+    // Ahead of a prefill launch (which starts while this one waits for its
+    // predecessor): one CTA per SM, so that a waiting append CTA never keeps
+    // a prefill CTA (168 x 352 registers) off an SM.
+    if ((pdl & kAppendTrigger) && blocks > 148) blocks = 148;
     if (!(pdl & kAppendDependent)) {
         kv_append_kernel<<<(unsigned)blocks, kAppendWarps * 32, 0, stream>>>(a);
         return cudaGetLastError();

@@ -271,6 +271,19 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     // writes (pages, table) or that came before it (Q) is read until it has
     // completed.
     if (!a.wait_at_end) asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Once this thread's tiles are done: let the next launch start (a kernel
+    // that does not wait for this one is never launched as its programmatic
+    // dependent). Reading the chunk's own tiles from its inputs, wait first
+    // for the previous kernel (the chunk's append): the output stores, which
+    // follow, must not overtake the previous chunk's, and the grid must not
+    // complete before that append has (the next chunk reads its pages).
+    // Every thread waiting before it triggers also makes "all of this grid
+    // triggered" imply "the append before it completed", which is what lets
+    // the next chunk's prefill start during this one's tail.
+    auto launch_next = [&] {
+        if (a.wait_at_end) asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    };
     PROBE_EE(1);
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
@@ -447,7 +460,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
-        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        launch_next();
         if (n_split > 1)  // the consumers' cluster barrier (every CTA's MMAs done)
             asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
         tc::fence_before_sync();
@@ -486,7 +499,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             if (!ok) atomicOr(a.err, kErrTimeout);
         }
         __syncwarp();
-        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        launch_next();
         if (n_split > 1)  // the consumers' cluster barrier (every CTA's MMAs done)
             asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
         tc::fence_before_sync();
@@ -659,9 +672,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     m_run = Mg;
     l_run = (n_tiles > 0 ? l0 * f0 : 0.f) + (n_tiles > 1 ? l1 * f1 : 0.f);
     PROBE_EE(5);
-    // The next kernel may start launching (a kernel that does not wait for
-    // this one is never launched as its programmatic dependent).
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    launch_next();
     // Reduce-scatter over the cluster: CTA k finalises and stores query rows
     // [k * 128 / n, (k + 1) * 128 / n). Each CTA writes the partials of the
     // rows it does not own into its own (idle) shared memory and sends each
@@ -808,10 +819,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
     PROBE_EE(7);
     if (!ok) atomicOr(a.err, kErrTimeout);
-    // The grid completes only after the previous kernel has (whatever reads
-    // this launch's output, or the pages that kernel wrote, waits for this
-    // one).
-    if (a.wait_at_end && tid == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
     tc::fence_before_sync();
     __syncthreads();
     PROBE_EE(3);
