@@ -106,14 +106,15 @@ constexpr int kThreadsTc = kConsumerThreads + 96;
 constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
 
 #ifdef GKV_PROBE_TIMELINE
-// Measurement builds only: per-tile phase clocks of threads 0 and 128 of the
-// first CTA of the grid.
+// Measurement builds only: per-tile phase clocks of threads 0 and 128 (the
+// two softmax groups), of the MMA warp and of the K-load warp, in one CTA.
 __device__ long long g_probe_pf[2 * 128 * 16];
 __device__ long long g_probe_mma[128 * 4];
 __device__ long long g_probe_ld[128 * 8];
 // Per CTA: entry, setup done, first S ready, exit, every MMA done, groups
-// merged, cluster merged, output stored, first cluster barrier passed,
-// DSMEM sends issued, second cluster barrier passed.
+// merged, partials merged, output stored, cluster barrier passed, partial
+// copies issued, own rows' partials received, output rows staged, staging
+// synchronised, reciprocal ready.
 __device__ unsigned long long g_probe_ee[1024 * 16];
 #define PROBE_EE(k)                                                                                          \
     if (tid == 0) {                                                                                          \
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     uint64_t* bar_o = bar_s + 2;             // [2] P V into O of a group done
     uint64_t* bar_p = bar_o + 2;             // [2] a group's 4 warps: P of its tile written (S read)
     uint64_t* bar_fin = bar_p + 2;           // every MMA of the CTA done
-    uint64_t* bar_recv = bar_fin + 1;        // cluster leader: the other CTAs' partials landed
+    uint64_t* bar_recv = bar_fin + 1;        // KV split: the other CTAs' partials of this CTA's rows landed
     constexpr int kNumBars = 9 + 4 * kStages;  // q, k, v, kfree, vfree, s[2], o[2], p[2], fin, recv
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + kNumBars);
 
@@ -232,7 +233,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int kv_end = a.causal ? last_q_abs + 1 : a.total;
     const int n_tiles_all = (kv_end + kBN - 1) / kBN;
     // KV split across the CTAs of a cluster (grid z = cluster size): this CTA
-    // takes tiles [j0, j0 + n_tiles) and the leader merges the results.
+    // takes tiles [j0, j0 + n_tiles); the CTAs then reduce-scatter their
+    // partials, each finalising a share of the rows.
     const int rank = blockIdx.z, n_split = gridDim.z;
     const int j0 = rank * n_tiles_all / n_split;
     const int n_tiles = (rank + 1) * n_tiles_all / n_split - j0;
