@@ -240,20 +240,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int n_tiles = (rank + 1) * n_tiles_all / n_split - j0;
 
     PROBE_EE(0);
+    // Page ids of tile j: 8 independent table loads (one latency, not 8),
+    // fetched by the issuing thread a tile before they are needed.
+    auto load_ids = [&](int j, int2 (&e)[kPagesPerTile]) {
+#pragma unroll
+        for (int i = 0; i < kPagesPerTile; ++i) {
+            int lp = (j0 + j) * kPagesPerTile + i;
+            if (lp >= a.n_pages) lp = a.n_pages - 1;  // beyond the cache: rows are masked / zeroed
+            // The chunk's own tiles come from its inputs; their entries may
+            // still be in the append's hands.
+            e[i] = j0 + j >= a.new_tile0 ? make_int2(0, 0) : a.table[lp];
+        }
+    };
     // The load warps fetch the first tile's page ids before the setup below
     // when nothing the previous kernel writes is read (wait_at_end): the
     // table load's latency then overlaps TMEM allocation and barrier setup.
     int2 ids_pre[kPagesPerTile];
     const bool pre = (warp == kLoadWarp || warp == kLoadWarp + 1) && (tid & 31) == 0 && n_tiles > 0 && !a.contig &&
                      a.wait_at_end;
-    if (pre) {
-#pragma unroll
-        for (int i = 0; i < kPagesPerTile; ++i) {
-            int lp = j0 * kPagesPerTile + i;
-            if (lp >= a.n_pages) lp = a.n_pages - 1;
-            ids_pre[i] = j0 >= a.new_tile0 ? make_int2(0, 0) : a.table[lp];
-        }
-    }
+    if (pre) load_ids(0, ids_pre);
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
@@ -299,18 +304,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     uint64_t pol_kv;
     asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol_kv));
 
-    // Page ids of tile j: 8 independent table loads (one latency, not 8),
-    // fetched by the issuing thread a tile before they are needed.
-    auto load_ids = [&](int j, int2 (&e)[kPagesPerTile]) {
-#pragma unroll
-        for (int i = 0; i < kPagesPerTile; ++i) {
-            int lp = (j0 + j) * kPagesPerTile + i;
-            if (lp >= a.n_pages) lp = a.n_pages - 1;  // beyond the cache: rows are masked / zeroed
-            // The chunk's own tiles come from its inputs; their entries may
-            // still be in the append's hands.
-            e[i] = j0 + j >= a.new_tile0 ? make_int2(0, 0) : a.table[lp];
-        }
-    };
     // Stage tile j's K (which = 0) or V (which = 1) into stage j % kStages.
     // Eight pages with consecutive ids are one run: two copies (one per
     // 64-dim half) with box {64, 1, 128} instead of 8 pages x 2 halves of box
